@@ -1,0 +1,436 @@
+"""Benchmark of the paged-attention hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: BF16 batched paged decode at
+Qwen2.5-0.5B attention geometry — 24 layers, 14 Q / 2 KV heads, head_dim 64,
+block_size 16, batch 64 per GPU with context lengths U[128, 4096], seeded
+random block tables over a pool of total blocks + 10 %, Q/K/V ~ N(0, 1) in
+BF16.  One step = for every layer, the batched KV write of the new token
+(PagedKVCache.write_slots) followed by batched paged decode
+(paged_attention_decode_batch_parallel) — the reference's per-layer hot path
+(model/qwen2.py:608-621).  Per step the KV pools stream ~1.66 GB, far above the
+126 MB L2, so no flush is needed between steps.
+
+Multi-GPU: one process per GPU (torchrun), requests sharded by rank with no
+communication (weak scaling: every rank decodes its own batch of 64).
+
+The JSON line: ``value`` = whole-job algorithmic KV bytes per second (device
+time, inputs resident); ``e2e`` = the same metric through the public API with
+the step's inputs copied from pinned host memory and the outputs copied back
+inside the timed region; ``roofline`` for the decode kernel; ``cpu_baseline``
+= the oracle port on the host cores (rank 0, N=1).
+
+``--impl reference`` times the reference's algorithm on the host CPU (the
+oracle port; the reference is PyTorch code with no compiled path to build) on
+a bounded sample of the same workload: one layer of the batch per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+
+# Workload constants.
+LAYERS, HQ, HKV, D, BS, BATCH = 24, 14, 2, 64, 16, 64
+CTX_LO, CTX_HI = 128, 4096
+METRIC = "paged-decode KV GB/s"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (KeyError, ValueError):
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def make_metadata(seed: int):
+    """Seeded contexts / block tables / slots for one rank's batch (numpy)."""
+    rng = np.random.default_rng(seed)
+    ctx = rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int64)
+    need = (ctx + BS - 1) // BS
+    nb = int(math.ceil(need.sum() * 1.1))
+    perm = rng.permutation(nb)
+    width = int(need.max())
+    tables = np.full((BATCH, width), -1, dtype=np.int64)
+    cur = 0
+    for b in range(BATCH):
+        tables[b, : need[b]] = perm[cur : cur + need[b]]
+        cur += need[b]
+    pos = ctx - 1
+    slots = tables[np.arange(BATCH), pos // BS] * BS + pos % BS
+    return ctx, tables, slots, nb
+
+
+def algorithmic_bytes(ctx: np.ndarray) -> dict:
+    """Bytes the decode step must move per layer (BF16):
+    KV reads sum(ctx) * Hkv * D * 2 B * 2 (K and V), Q reads and O writes
+    B * Hq * D * 2 B each, block-table reads sum(ceil(ctx/16)) * 8 B, and the
+    new-token KV write B * Hkv * D * 2 B * 2."""
+    kv = int(ctx.sum()) * HKV * D * 2 * 2
+    qo = 2 * BATCH * HQ * D * 2
+    table = int(((ctx + BS - 1) // BS).sum()) * 8
+    scatter = BATCH * HKV * D * 2 * 2
+    return {"kv": kv, "decode": kv + qo + table, "layer": kv + qo + table + scatter}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu_index), "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        try:
+            for line in Path(self.path).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        finally:
+            os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        if local_rank < len(ids) and ids[local_rank].isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+# ---------------------------------------------------------------------------
+# Reference arm: the reference's algorithm on the host CPU (oracle port)
+# ---------------------------------------------------------------------------
+
+
+def cpu_reference_sample(steps: int, warmup: int, seed: int = 0):
+    """Time the oracle port of paged_attention_decode_batch_parallel plus the
+    write_slots restatement on one layer of the workload per step."""
+    from oracle import paged_attention_oracle as O
+
+    ctx, tables, slots, nb = make_metadata(seed)
+    rng = np.random.default_rng(seed + 1)
+    k = rng.standard_normal((1, nb, BS, HKV, D), dtype=np.float32)
+    v = rng.standard_normal((1, nb, BS, HKV, D), dtype=np.float32)
+    q = O.round_to_bf16(rng.standard_normal((BATCH, HQ, D), dtype=np.float32))
+    nk = O.round_to_bf16(rng.standard_normal((BATCH, HKV, D), dtype=np.float32))
+    nv = O.round_to_bf16(rng.standard_normal((BATCH, HKV, D), dtype=np.float32))
+    threads = os.cpu_count() or 1
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        O.write_slots(k, v, slots, nk, nv, 0)
+        O.decode_batch_threaded(q, k[0], v[0], tables, ctx, BS, threads)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    per_layer = statistics.median(times)
+    gbs = algorithmic_bytes(ctx)["kv"] / per_layer / 1e9
+    return {
+        "value": gbs,
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"one layer of the config-2 batch (64 seqs, sum ctx {int(ctx.sum())}) per step, "
+                  f"median of {steps} steps, FP32 math on BF16-valued inputs",
+        "ms_per_layer": per_layer * 1e3,
+    }
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    r = cpu_reference_sample(args.steps, args.warmup)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": r["value"],
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": r["ms_per_layer"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "config2: bf16 batched paged decode, 24 layers, 14/2 heads, D64, bs16, "
+                               "batch 64, ctx U[128,4096] (one layer per step on the CPU)"},
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# Our arm
+# ---------------------------------------------------------------------------
+
+
+def build_rank_workload(rank: int, device):
+    from mini_llm_runtime_b200 import PagedKVCache
+
+    ctx, tables, slots, nb = make_metadata(1000 + rank)
+    cache = PagedKVCache(LAYERS, nb, BS, HKV, D, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(2000 + rank)
+    cache.k_cache.normal_(generator=g)
+    cache.v_cache.normal_(generator=g)
+    q = torch.randn(LAYERS, BATCH, HQ, D, device=device, generator=g).to(torch.bfloat16)
+    nk = torch.randn(LAYERS, BATCH, HKV, D, device=device, generator=g).to(torch.bfloat16)
+    nv = torch.randn(LAYERS, BATCH, HKV, D, device=device, generator=g).to(torch.bfloat16)
+    return {
+        "cache": cache,
+        "ctx": ctx,
+        "tables_np": tables,
+        "slots_np": slots,
+        "tables": torch.tensor(tables, device=device),
+        "lens": torch.tensor(ctx, device=device),
+        "slots": torch.tensor(slots, device=device),
+        "q": q,
+        "nk": nk,
+        "nv": nv,
+    }
+
+
+def device_step(w, out, ev_pairs=None):
+    """One step with inputs resident in HBM: per layer, KV write + decode.
+    ``out`` is a list that keeps each layer's output tensor."""
+    from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel as decode
+
+    cache = w["cache"]
+    for layer in range(LAYERS):
+        # The step's slot mapping was validated once when the batch was built.
+        cache.write_slots(w["slots"], w["nk"][layer], w["nv"][layer], layer, validate=False)
+        kc, vc = cache.k_cache[layer], cache.v_cache[layer]
+        if ev_pairs is not None:
+            ev_pairs[layer][0].record()
+        out[layer] = decode(w["q"][layer], kc, vc, w["tables"], w["lens"], BS)
+        if ev_pairs is not None:
+            ev_pairs[layer][1].record()
+
+
+def main():
+    args = parse_args()
+    rank, world, local_rank = env_rank()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    from mini_llm_runtime_b200 import _lib
+
+    _lib.load()
+
+    w = build_rank_workload(rank, device)
+    nbytes = algorithmic_bytes(w["ctx"])
+    out = [None] * LAYERS
+    w["cache"].validate_slots(w["slots"], w["nk"][0], w["nv"][0], 0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # ---- device-resident timing -------------------------------------------
+    for _ in range(max(args.warmup, 3)):
+        device_step(w, out)
+    ev_pairs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
+                for _ in range(args.steps)]
+    sampler = ClockSampler(physical_gpu_index(local_rank))
+    sampler.start()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for s in range(args.steps):
+        device_step(w, out, ev_pairs[s])
+    t1.record()
+    barrier()
+    clocks = sampler.stop()
+    ms_step = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    dec_ms = [p[0].elapsed_time(p[1]) for step in ev_pairs for p in step]
+    dec_avg_ms = statistics.mean(dec_ms)
+    total_kv = sum_over_ranks(nbytes["kv"] * LAYERS)
+    value = total_kv / (ms_step * 1e-3) / 1e9
+    tokens = sum_over_ranks(BATCH)
+
+    # ---- end-to-end through the public API with host buffers ----------------
+    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+    host = {"q": pin(w["q"]), "nk": pin(w["nk"]), "nv": pin(w["nv"]),
+            "tables": pin(w["tables"]), "lens": pin(w["lens"]), "slots": pin(w["slots"])}
+    host_out = torch.empty((LAYERS, BATCH, HQ, D), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = host_out.numel() * host_out.element_size()
+    dev_in = {k: torch.empty_like(v, device=device) for k, v in host.items()}
+
+    def e2e_step():
+        from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel as decode
+
+        for k in ("tables", "lens", "slots"):
+            dev_in[k].copy_(host[k], non_blocking=True)
+        cache = w["cache"]
+        for layer in range(LAYERS):
+            for k in ("q", "nk", "nv"):
+                dev_in[k][layer].copy_(host[k][layer], non_blocking=True)
+            cache.write_slots(dev_in["slots"], dev_in["nk"][layer], dev_in["nv"][layer], layer,
+                              validate=(layer == 0))
+            o = decode(dev_in["q"][layer], cache.k_cache[layer], cache.v_cache[layer], dev_in["tables"],
+                       dev_in["lens"], BS)
+            host_out[layer].copy_(o, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_value = total_kv / (e2e_ms * 1e-3) / 1e9
+
+    # ---- roofline of the decode kernel ------------------------------------
+    peak, peak_kind = hbm_peak()
+    achieved = nbytes["decode"] / (dec_avg_ms * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "decode_bf16_config2_traffic.txt"
+    if tfile.exists():
+        for line in tfile.read_text().splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                traffic = float(line.split(":", 1)[1])
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_reference_sample(steps=5, warmup=1)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(args.warmup, 3),
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "config2: bf16 batched paged decode (KV write + decode per layer), 24 layers, "
+                            "14/2 heads, D64, bs16, batch 64 per GPU, ctx U[128,4096], pool = blocks*1.1",
+                "global_batch": BATCH * world,
+                "parallelism": f"request-sharded dp{world}, no communication",
+                "l2": "inputs larger than L2 (1.66 GB of KV streamed per step per GPU), no flush",
+            },
+            "tok_per_s": tokens / (ms_step * 1e-3),
+            "frac_of_hbm_peak": value / world / peak,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": e2e_ms, "tok_per_s": tokens / (e2e_ms * 1e-3)},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "decode_fast_kernel<bf16,64>",
+                         "bytes_per_launch": nbytes["decode"], "avg_launch_ms": dec_avg_ms},
+            "gpu_launches": args.steps * LAYERS * 2,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * pagedattn.h — C ABI of libpagedattn.so, the B200 (sm_100a) paged-attention
+ * hot path of mini-llm-runtime.
+ *
+ * Conventions for every entry point:
+ *   - Pointers are device pointers unless stated otherwise; the caller owns
+ *     and allocates every buffer (outputs and workspaces included).  The
+ *     library never allocates device memory.
+ *   - Strides are in ELEMENTS.  The innermost (head_dim) dimension of every
+ *     tensor argument must be contiguous.
+ *   - `stream` is a cudaStream_t passed as void*.  Launches are asynchronous
+ *     on that stream; no entry point synchronises the host.
+ *   - The return value is PA_OK (0) or a negative PA_ERR_* code.  Argument
+ *     errors are detected on the host before anything is launched, so a
+ *     non-zero return means no device memory was modified.
+ *   - Block tables and context lengths are int64 (torch.long), matching the
+ *     reference's metadata tensors (model/qwen2.py:566-579).
+ *
+ * Citations are paths inside the mini-llm-runtime project
+ * (src/mini_llm_runtime/...).
+ */
+#ifndef PAGEDATTN_H_
+#define PAGEDATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PA_API __attribute__((visibility("default")))
+#else
+#define PA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define PA_OK 0
+#define PA_ERR_INVALID (-1)     /* bad shape / stride / size argument          */
+#define PA_ERR_UNSUPPORTED (-2) /* valid but not implemented (dtype, head_dim) */
+#define PA_ERR_CUDA (-3)        /* CUDA runtime reported a launch error        */
+#define PA_ERR_WORKSPACE (-4)   /* workspace missing or too small              */
+#define PA_ERR_CAPACITY (-5)    /* request exceeds a fixed built-in capacity   */
+
+/* Device-side status codes written into the workspace status word when a
+ * bounded wait inside a kernel gives up (never expected in normal runs). */
+#define PA_DEVICE_TIMEOUT_TMA 101
+#define PA_DEVICE_TIMEOUT_MMA 102
+
+/* Element types (torch dtype mapping in mini_llm_runtime_b200/_lib.py). */
+#define PA_DTYPE_F32 0
+#define PA_DTYPE_F16 1
+#define PA_DTYPE_BF16 2
+#define PA_DTYPE_F64 3
+
+/* Human-readable name of a status code (static storage). */
+PA_API const char* pa_status_string(int status);
+
+/* ABI version of this library; bumps when a signature changes. */
+PA_API int pa_abi_version(void);
+
+/*
+ * Batched KV-cache write: scatter rows k[t], v[t] ([num_kv_heads, head_dim])
+ * into flat slot slot_mapping[t] of one layer's pools, converting to the pool
+ * dtype with round-to-nearest-even exactly as torch's `.to(dtype)` does.
+ *
+ * Replaces PagedKVCache.write_slots (runtime/paged_kv_cache.py:194-249):
+ * the two `index_copy_` calls at :243-249.  The range / duplicate checks at
+ * :228-239 stay on the host (the Python mirror runs them before calling).
+ *
+ * k, v          : [T, Hkv, D] with element strides (s0, s1, s2) of src_dtype
+ *                 (F32/F16/BF16/F64), any layout.
+ * slot_mapping  : [T] int32 (slot_is_int64 = 0) or int64 (slot_is_int64 = 1)
+ * k_pool_layer  : this layer's pool viewed as [num_slots, Hkv, D] contiguous,
+ *                 num_slots = num_blocks * block_size (slot = block*bs + off).
+ * Slots outside [0, num_slots) are skipped on the device (never written).
+ */
+PA_API int pa_kv_scatter(const void* k, int64_t k_s0, int64_t k_s1, int64_t k_s2, const void* v, int64_t v_s0,
+                  int64_t v_s1, int64_t v_s2, int src_dtype, const void* slot_mapping, int slot_is_int64,
+                  int64_t num_tokens, void* k_pool_layer, void* v_pool_layer, int64_t num_slots,
+                  int num_kv_heads, int head_dim, int pool_dtype, void* stream);
+
+/*
+ * Bytes of workspace pa_paged_decode needs for `max_splits` KV partitions
+ * per sequence.  The workspace must be zero-filled once when allocated; the
+ * kernels leave it ready for the next call (split tickets are reset by the
+ * CTA that consumes them).  Calls that share one workspace must be ordered
+ * on the same stream.
+ */
+PA_API size_t pa_decode_workspace_size(int batch, int num_q_heads, int head_dim, int max_splits);
+
+/*
+ * Number of KV partitions per sequence pa_paged_decode will use for these
+ * arguments (partition_tokens = 0 selects the automatic size).  Lets the
+ * caller size the workspace exactly.
+ */
+PA_API int pa_decode_num_splits(int batch, int num_kv_heads, int num_q_heads, int head_dim, int block_size,
+                         int64_t bt_width, int partition_tokens, int dtype);
+
+/*
+ * Batched single-token paged decode with split-KV and a log-sum-exp merge.
+ *
+ *   out[b, h, :] = softmax(scale * q[b, h] . K_b^T) V_b
+ * where K_b, V_b are the first context_lens[b] tokens of sequence b gathered
+ * through block_tables[b] from the layer pools [num_blocks, block_size, Hkv, D]
+ * and q head h reads KV head h / (Hq / Hkv) (GQA / MQA).
+ *
+ * Replaces paged_attention_decode_batch_parallel
+ * (kernels/reference/paged_attention.py:178-254) — same inputs, same output
+ * [B, Hq, D] in the input dtype — and, with partition_tokens > 0, the Triton
+ * split-KV stage-1 + merge pair (kernels/triton/paged_attention.py:24-213,
+ * :528-700, :1530-1618) generalised to a batch.
+ *
+ * q            : [B, Hq, D], element strides (q_s0, q_s1), last dim contiguous
+ * block_tables : [B, bt_width] int64, row stride bt_stride; entries past a
+ *                sequence's last block are ignored (the reference pads -1)
+ * context_lens : [B] int64, includes the token being decoded (> 0)
+ * out          : [B, Hq, D], element strides (o_s0, o_s1)
+ * dtype        : F32, F16 or BF16 for q, pools and out (all the same)
+ * partition_tokens : KV tokens per split (0 = automatic); rounded up to a
+ *                multiple of 16.  A sequence shorter than one partition is
+ *                finished in a single CTA without touching the workspace.
+ * workspace    : >= pa_decode_workspace_size(B, Hq, D, splits) bytes, zeroed
+ *                once at allocation.
+ */
+PA_API int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_layer,
+                    const void* v_pool_layer, int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                    const int64_t* block_tables, int64_t bt_stride, int64_t bt_width, const int64_t* context_lens,
+                    void* out, int64_t o_s0, int64_t o_s1, int batch, int num_q_heads, float scale, int dtype,
+                    int partition_tokens, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Causal chunk-prefill over a paged cache, batched over sequences.
+ *
+ * Sequence s owns packed query rows [cu_q_lens[s], cu_q_lens[s+1]) of q; its
+ * chunk is the last (cu_q_lens[s+1]-cu_q_lens[s]) tokens of a context of
+ * context_lens[s] tokens (prefix = context_len - chunk_len).  Query i of the
+ * chunk attends to cached keys at absolute positions <= prefix + i.  The
+ * chunk's own K/V must already be in the pools (written by pa_kv_scatter).
+ *
+ * Replaces paged_attention_prefill_chunk_tiled and its dense reference
+ * (kernels/reference/paged_attention.py:282-434); the single-request
+ * signature is the nseq = 1 case.  BF16/F16 run on tcgen05 tensor cores with
+ * the accumulators in tensor memory; F32 runs on CUDA cores.
+ *
+ * q            : [total_q, Hq, D], element strides (q_s0, q_s1)
+ * cu_q_lens    : [num_seqs + 1] int64 (query_start_loc, model_runner.py:14-27)
+ * context_lens : [num_seqs] int64
+ * block_tables : [num_seqs, bt_width] int64, row stride bt_stride
+ * out          : [total_q, Hq, D], element strides (o_s0, o_s1)
+ * max_q_len    : upper bound of any chunk length (sizes the launch grid)
+ */
+PA_API int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
+                     const int64_t* context_lens, const int64_t* block_tables, int64_t bt_stride,
+                     int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer, int64_t num_blocks,
+                     int block_size, int num_kv_heads, int head_dim, void* out, int64_t o_s0, int64_t o_s1,
+                     int num_seqs, int64_t total_q, int max_q_len, int num_q_heads, float scale, int dtype,
+                     void* stream);
+
+/*
+ * FP32 P.V accumulator: out[b, d] = sum_n p[b, n] * v[b, n, d] for N = 64,
+ * D = 256, contiguous inputs.
+ *
+ * Replaces paged_attention_accumulator_cuda
+ * (kernels/cuda/accumulator.py:21-37 -> paged_attention_accumulator.cu:72-90).
+ */
+PA_API int pa_accumulate_pv(const float* p, const float* v, float* out, int64_t batch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGEDATTN_H_ */

@@ -1,0 +1,26 @@
+"""B200-native (sm_100a) paged-attention hot path for mini-llm-runtime.
+
+Drop-in replacements for the reference's paged-attention ops and
+``PagedKVCache.write_slots``; every op runs a hand-written CUDA kernel from
+``libpagedattn.so`` through its C ABI (include/pagedattn.h).
+"""
+
+from .paged_attention import (
+    paged_attention_accumulator_cuda,
+    paged_attention_decode,
+    paged_attention_decode_batch_parallel,
+    paged_attention_decode_split_kv,
+    paged_attention_prefill_chunk_tiled,
+    paged_attention_prefill_varlen,
+)
+from .paged_kv_cache import PagedKVCache
+
+__all__ = [
+    "PagedKVCache",
+    "paged_attention_accumulator_cuda",
+    "paged_attention_decode",
+    "paged_attention_decode_batch_parallel",
+    "paged_attention_decode_split_kv",
+    "paged_attention_prefill_chunk_tiled",
+    "paged_attention_prefill_varlen",
+]

@@ -1,0 +1,134 @@
+"""ctypes binding of libpagedattn.so (the C ABI declared in include/pagedattn.h).
+
+The library is built in-tree by ``python -m mini_llm_runtime_b200.build``.
+Loading fails loudly when it is missing: there is no CPU or PyTorch fallback
+for any op in this package.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "libpagedattn.so"
+
+PA_OK = 0
+PA_ERR_INVALID = -1
+PA_ERR_UNSUPPORTED = -2
+PA_ERR_CUDA = -3
+PA_ERR_WORKSPACE = -4
+PA_ERR_CAPACITY = -5
+
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+_size = ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/pagedattn.h
+SIGNATURES: dict[str, tuple] = {
+    "pa_status_string": (ctypes.c_char_p, [_i32]),
+    "pa_abi_version": (_i32, []),
+    "pa_kv_scatter": (
+        _i32,
+        [_c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p, _i32, _i64,
+         _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p],
+    ),
+    "pa_decode_workspace_size": (_size, [_i32, _i32, _i32, _i32]),
+    "pa_decode_num_splits": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i32, _i32]),
+    "pa_paged_decode": (
+        _i32,
+        [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i64, _i64,
+         _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _f32, _i32, _i32, _c_void_p, _size, _c_void_p],
+    ),
+    "pa_chunk_prefill": (
+        _i32,
+        [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64,
+         _i32, _i32, _i32, _c_void_p, _i64, _i64, _i32, _i64, _i32, _i32, _f32, _i32, _c_void_p],
+    ),
+    "pa_accumulate_pv": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class PagedAttentionError(RuntimeError):
+    """A libpagedattn entry point returned a non-zero status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load libpagedattn.so once and attach the ctypes signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise PagedAttentionError(
+                    f"{LIB_PATH} is missing; build it with `python -m mini_llm_runtime_b200.build` "
+                    "(there is no CPU fallback)"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != PA_OK:
+        msg = load().pa_status_string(status).decode()
+        raise PagedAttentionError(f"{what} failed: {msg} (status {status})")
+
+
+def require_cuda(*tensors: torch.Tensor, what: str) -> torch.device:
+    """The product path runs only on CUDA tensors; anything else is an error."""
+    dev = None
+    for t in tensors:
+        if not t.is_cuda:
+            raise PagedAttentionError(
+                f"{what} requires CUDA tensors (got a tensor on {t.device}); "
+                "this package has no CPU fallback"
+            )
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise PagedAttentionError(f"{what}: all tensors must be on one device")
+    return dev
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODES[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}") from None
+
+
+# ---------------------------------------------------------------------------
+# Decode workspace: one zero-initialised buffer per (device, stream), grown on
+# demand.  The kernels restore their split tickets to zero, so a buffer stays
+# valid across calls; calls on one stream are ordered, so they never overlap.
+# ---------------------------------------------------------------------------
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def decode_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        # Zeroed on the current stream, so it is ready before the next launch.
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws

@@ -1,0 +1,182 @@
+"""Decode parity on the GPU: the CUDA kernels (through the C ABI) against the
+oracle and the reference's golden vectors.
+
+Tolerances (north_star): FP32 within 1e-5 relative (atol 1e-6); BF16/F16
+within 2e-2 absolute / 1e-2 relative of the FP32 reference run on the
+up-cast inputs."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from mini_llm_runtime_b200 import (
+    PagedKVCache,
+    paged_attention_decode,
+    paged_attention_decode_batch_parallel,
+    paged_attention_decode_split_kv,
+)
+from oracle import paged_attention_oracle as O
+from tests.paged_inputs import make_decode_case
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = {
+    torch.float32: dict(rtol=1e-5, atol=1e-6),
+    torch.bfloat16: dict(rtol=1e-2, atol=2e-2),
+    torch.float16: dict(rtol=1e-2, atol=2e-2),
+}
+
+
+def check(actual: torch.Tensor, expected: np.ndarray, dtype):
+    a = actual.float().cpu().numpy()
+    assert np.isfinite(a).all(), "NaN/Inf in kernel output"
+    np.testing.assert_allclose(a, expected, **TOL[dtype])
+
+
+def oracle_decode(case):
+    q, k, v, tables, lens = case["np"]
+    return O.decode_batch(q, k, v, tables, lens, case["bs"])
+
+
+def test_golden_config1_fp32(cuda_device):
+    """Config 1 end to end: write the new tokens through write_slots, then
+    decode; both match the reference's recorded outputs."""
+    g = np.load(GOLDEN / "decode_config1.npz")
+    bs = int(g["block_size"])
+    k_pool = torch.tensor(g["k_pool"])
+    v_pool = torch.tensor(g["v_pool"])
+    slots = torch.tensor(g["slot_mapping"])
+    k_pool.flatten(1, 2)[0, slots] = torch.tensor(g["old_k_at_slots"])
+    v_pool.flatten(1, 2)[0, slots] = torch.tensor(g["old_v_at_slots"])
+    cache = PagedKVCache(1, k_pool.shape[1], bs, 2, 64, dtype=torch.float32, device=cuda_device)
+    cache.k_cache.copy_(k_pool)
+    cache.v_cache.copy_(v_pool)
+    cache.write_slots(slots.to(cuda_device), torch.tensor(g["new_k"]).to(cuda_device),
+                      torch.tensor(g["new_v"]).to(cuda_device), layer_idx=0)
+    assert torch.equal(cache.k_cache.cpu(), torch.tensor(g["k_pool"]))
+    assert torch.equal(cache.v_cache.cpu(), torch.tensor(g["v_pool"]))
+    kc, vc = cache.get_layer_cache(0)
+    out = paged_attention_decode_batch_parallel(
+        torch.tensor(g["q"]).to(cuda_device), kc, vc, torch.tensor(g["block_tables"]).to(cuda_device),
+        torch.tensor(g["context_lens"]).to(cuda_device), bs)
+    check(out, g["out"], torch.float32)
+
+
+def test_golden_small_cases(cuda_device):
+    g = np.load(GOLDEN / "decode_small.npz")
+    for i in range(int(g["num_cases"])):
+        t = lambda n: torch.tensor(g[f"c{i}_{n}"]).to(cuda_device)  # noqa: E731
+        out = paged_attention_decode_batch_parallel(t("q"), t("k"), t("v"), t("tables"), t("lens"), 2)
+        check(out, g[f"c{i}_out"], torch.float32)
+
+
+def test_golden_bf16_against_fp32_reference(cuda_device):
+    g = np.load(GOLDEN / "decode_bf16.npz")
+
+    def bf(name):
+        return torch.tensor(g[name].view(np.int16)).view(torch.bfloat16).to(cuda_device)
+
+    out = paged_attention_decode_batch_parallel(
+        bf("q_bits"), bf("k_pool_bits"), bf("v_pool_bits"), torch.tensor(g["block_tables"]).to(cuda_device),
+        torch.tensor(g["context_lens"]).to(cuda_device), int(g["block_size"]))
+    assert out.dtype == torch.bfloat16
+    check(out, g["out_fp32_reference"], torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv", [(14, 2), (4, 4), (8, 1), (28, 4), (32, 8)], ids=["gqa7", "mha", "mqa", "gqa7x4", "gqa4"])
+@pytest.mark.parametrize("d", [64, 128])
+def test_decode_geometries(cuda_device, dtype, hq, hkv, d):
+    ctx = [1, 15, 16, 17, 63, 64, 65, 127, 128, 255, 513, 700]
+    case = make_decode_case(ctx, hq, hkv, d, 16, dtype, cuda_device, seed=hq * 7 + d)
+    out = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+    check(out, oracle_decode(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("d", [8, 16, 40, 80, 96, 160])
+def test_decode_odd_head_dims(cuda_device, dtype, d):
+    """Head dims outside the tensor-core set (Triton test grid,
+    tests/kernels/test_paged_attention_triton.py:418-427)."""
+    case = make_decode_case([1, 33, 129, 600], 8, 2, d, 16, dtype, cuda_device, seed=d)
+    out = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+    check(out, oracle_decode(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("bs", [2, 3, 8, 32, 64])
+def test_decode_block_sizes(cuda_device, dtype, bs):
+    case = make_decode_case([1, 5, 31, 64, 200], 14, 2, 64, bs, dtype, cuda_device, seed=bs, reverse_tables=True)
+    out = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], bs)
+    check(out, oracle_decode(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("seq_len", list(range(1, 66)))
+def test_decode_tile_boundaries(cuda_device, dtype, seq_len):
+    """Every length 1..65 (test_paged_attention_triton.py:406-415)."""
+    case = make_decode_case([seq_len, 65 - seq_len + 1], 14, 2, 64, 16, dtype, cuda_device, seed=seq_len)
+    out = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+    check(out, oracle_decode(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("partition", [16, 64, 128, 512, 2048])
+def test_split_kv_partitions(cuda_device, dtype, partition):
+    """Split-KV at partition edges (seq lens 513 / 529 / 600 / 4096 / 4097)."""
+    case = make_decode_case([513, 529, 600, 4096, 4097, 1], 14, 2, 64, 16, dtype, cuda_device, seed=partition)
+    out = paged_attention_decode_split_kv(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16,
+                                          partition_size=partition)
+    check(out, oracle_decode(case), dtype)
+    # Tickets reset: a second call on the same workspace gives the same result.
+    out2 = paged_attention_decode_split_kv(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16,
+                                           partition_size=partition)
+    assert torch.equal(out, out2)
+
+
+def test_split_kv_single_sequence_signature(cuda_device):
+    """The Triton-style single-sequence call (q [Hq, D], list table, int len)."""
+    case = make_decode_case([3000], 32, 8, 128, 16, torch.float16, cuda_device, seed=5, reverse_tables=True)
+    table = case["tables"][0].tolist()
+    out = paged_attention_decode_split_kv(case["q"][0], case["k"], case["v"], table, 3000, 16, partition_size=128)
+    check(out, oracle_decode(case)[0], torch.float16)
+
+
+def test_single_decode_api(cuda_device):
+    case = make_decode_case([37], 14, 2, 64, 16, torch.float32, cuda_device, seed=9)
+    table = case["tables"][0].tolist()
+    out = paged_attention_decode(case["q"][0], case["k"], case["v"], table, 37, 16)
+    check(out, oracle_decode(case)[0], torch.float32)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_config2_full_size(cuda_device, dtype):
+    """BASELINE config 2 geometry at full size (one layer): B=64, contexts
+    U[128, 4096], 14/2 heads, D=64, bs=16, pool = total blocks + 10%."""
+    rng = np.random.default_rng(0)
+    ctx = rng.integers(128, 4097, size=64).tolist()
+    need = sum((c + 15) // 16 for c in ctx)
+    case = make_decode_case(ctx, 14, 2, 64, 16, dtype, cuda_device, seed=2, extra_blocks=need // 10)
+    out = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+    check(out, oracle_decode(case), dtype)
+
+
+def test_config3_long_context_split(cuda_device):
+    """BASELINE config 3 shape at reduced batch: 32768-token contexts split
+    into 16 partitions of 2048, LSE-merged."""
+    case = make_decode_case([32768, 32768], 14, 2, 64, 16, torch.bfloat16, cuda_device, seed=3, extra_blocks=10)
+    out = paged_attention_decode_split_kv(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16,
+                                          partition_size=2048)
+    check(out, oracle_decode(case), torch.bfloat16)
+
+
+def test_decode_is_deterministic_and_does_not_write_pools(cuda_device):
+    case = make_decode_case([100, 2000, 5], 14, 2, 64, 16, torch.bfloat16, cuda_device, seed=11)
+    k0, v0 = case["k"].clone(), case["v"].clone()
+    a = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+    b = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+    assert torch.equal(a, b)
+    assert torch.equal(k0.view(torch.int16), case["k"].view(torch.int16))
+    assert torch.equal(v0.view(torch.int16), case["v"].view(torch.int16))

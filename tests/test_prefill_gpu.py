@@ -1,0 +1,122 @@
+"""Chunk-prefill parity on the GPU against the oracle and the reference's
+golden vectors (FP32 1e-5 relative; BF16 2e-2 abs / 1e-2 rel vs FP32)."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from mini_llm_runtime_b200 import (
+    PagedKVCache,
+    paged_attention_prefill_chunk_tiled,
+    paged_attention_prefill_varlen,
+)
+from oracle import paged_attention_oracle as O
+from tests.paged_inputs import make_prefill_case
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = {
+    torch.float32: dict(rtol=1e-5, atol=1e-6),
+    torch.bfloat16: dict(rtol=1e-2, atol=2e-2),
+    torch.float16: dict(rtol=1e-2, atol=2e-2),
+}
+
+
+def check(actual, expected, dtype):
+    a = actual.float().cpu().numpy()
+    assert np.isfinite(a).all(), "NaN/Inf in kernel output"
+    np.testing.assert_allclose(a, expected, **TOL[dtype])
+
+
+def oracle_prefill(case):
+    _, k, v, tables, _ = case["np"]
+    outs = []
+    for s, (p, c) in enumerate(zip(case["prefix"], case["chunk"])):
+        q = case["q_np"][case["cu_np"][s] : case["cu_np"][s + 1]]
+        outs.append(O.prefill_chunk(q, k, v, tables[s], p, p + c, case["bs"]))
+    return np.concatenate(outs, 0)
+
+
+def test_golden_small_grid(cuda_device):
+    """tests/kernels/test_paged_attention.py:249-351 cases (bs 3, NaN pools)."""
+    g = np.load(GOLDEN / "prefill_small.npz")
+    for i in range(int(g["num_cases"])):
+        prefix, ctx, bs, tile = (int(x) for x in g[f"c{i}_meta"])
+        t = lambda n: torch.tensor(g[f"c{i}_{n}"]).to(cuda_device)  # noqa: E731
+        out = paged_attention_prefill_chunk_tiled(t("q"), t("k"), t("v"), g[f"c{i}_table"].tolist(), prefix, ctx,
+                                                  bs, tile)
+        assert out.shape == t("q").shape and out.dtype == torch.float32
+        check(out, g[f"c{i}_out"], torch.float32)
+
+
+def test_golden_medium(cuda_device):
+    g = np.load(GOLDEN / "prefill_medium.npz")
+    prefix, ctx, bs = (int(x) for x in g["meta"])
+    t = lambda n: torch.tensor(g[n]).to(cuda_device)  # noqa: E731
+    out = paged_attention_prefill_chunk_tiled(t("q"), t("k"), t("v"), torch.tensor(g["table"]), prefix, ctx, bs, 16)
+    check(out, g["out"], torch.float32)
+
+    def bf(name):
+        return torch.tensor(g[name].view(np.int16)).view(torch.bfloat16).to(cuda_device)
+
+    outb = paged_attention_prefill_chunk_tiled(bf("q_bits"), bf("k_bits"), bf("v_bits"), g["table"].tolist(),
+                                               prefix, ctx, bs, 16)
+    check(outb, g["out_bf16_inputs_fp32_reference"], torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv", [(14, 2), (4, 4), (8, 1)], ids=["gqa7", "mha", "mqa"])
+@pytest.mark.parametrize("d", [64, 128])
+def test_varlen_batch(cuda_device, dtype, hq, hkv, d):
+    prefix = [0, 5, 16, 200, 37, 0]
+    chunk = [1, 17, 128, 130, 64, 300]
+    case = make_prefill_case(prefix, chunk, hq, hkv, d, 16, dtype, cuda_device, seed=hq + d)
+    out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
+                                         case["max_q"])
+    check(out, oracle_prefill(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("d,bs", [(8, 16), (40, 16), (64, 3), (64, 8), (96, 32), (64, 64)])
+def test_odd_shapes(cuda_device, dtype, d, bs):
+    case = make_prefill_case([0, 9, 50], [7, 33, 65], 8, 2, d, bs, dtype, cuda_device, seed=d * bs)
+    out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
+                                         case["max_q"])
+    check(out, oracle_prefill(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_config4_geometry(cuda_device, dtype):
+    """BASELINE config 4 at reduced batch: prefix U[0, 2048], 512-token chunks,
+    14/2 heads, D 64, bs 16, new K/V scattered through the slot mapping first."""
+    rng = np.random.default_rng(4)
+    nseq = 4
+    prefix = rng.integers(0, 2049, size=nseq).tolist()
+    chunk = [512] * nseq
+    case = make_prefill_case(prefix, chunk, 14, 2, 64, 16, dtype, cuda_device, seed=4)
+    # Rewrite the chunks' K/V through write_slots to exercise the whole path.
+    k_pool, v_pool = case["k"], case["v"]
+    nb = k_pool.shape[0]
+    cache = PagedKVCache(1, nb, 16, 2, 64, dtype=dtype, device=cuda_device)
+    cache.k_cache[0].copy_(k_pool)
+    cache.v_cache[0].copy_(v_pool)
+    g = torch.Generator().manual_seed(44)
+    slots, ks, vs = [], [], []
+    for s in range(nseq):
+        tbl = case["tables"][s].tolist()
+        for pos in range(prefix[s], prefix[s] + chunk[s]):
+            slots.append(tbl[pos // 16] * 16 + pos % 16)
+    new_k = torch.randn(len(slots), 2, 64, generator=g).to(dtype)
+    new_v = torch.randn(len(slots), 2, 64, generator=g).to(dtype)
+    cache.write_slots(torch.tensor(slots, device=cuda_device), new_k.to(cuda_device), new_v.to(cuda_device), 0)
+    kc, vc = cache.get_layer_cache(0)
+    out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], kc, vc, 512)
+    k_np = kc.float().cpu().numpy()
+    v_np = vc.float().cpu().numpy()
+    exp = []
+    for s in range(nseq):
+        q = case["q_np"][case["cu_np"][s] : case["cu_np"][s + 1]]
+        exp.append(O.prefill_chunk(q, k_np, v_np, case["np"][3][s], prefix[s], prefix[s] + 512, 16))
+    check(out, np.concatenate(exp, 0), dtype)
