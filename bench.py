@@ -243,38 +243,26 @@ def build_rank_workload(rank: int, device):
     g = torch.Generator(device=device).manual_seed(2000 + rank)
     cache.k_cache.normal_(generator=g)
     cache.v_cache.normal_(generator=g)
-    q = torch.randn(LAYERS, BATCH, HQ, D, device=device, generator=g).to(torch.bfloat16)
-    nk = torch.randn(LAYERS, BATCH, HKV, D, device=device, generator=g).to(torch.bfloat16)
-    nv = torch.randn(LAYERS, BATCH, HKV, D, device=device, generator=g).to(torch.bfloat16)
-    return {
-        "cache": cache,
-        "ctx": ctx,
-        "tables_np": tables,
-        "slots_np": slots,
-        "tables": torch.tensor(tables, device=device),
-        "lens": torch.tensor(ctx, device=device),
-        "slots": torch.tensor(slots, device=device),
-        "q": q,
-        "nk": nk,
-        "nv": nv,
+    gen = torch.Generator().manual_seed(3000 + rank)
+    inputs = {
+        "q": torch.randn(LAYERS, BATCH, HQ, D, generator=gen).to(torch.bfloat16),
+        "new_k": torch.randn(LAYERS, BATCH, HKV, D, generator=gen).to(torch.bfloat16),
+        "new_v": torch.randn(LAYERS, BATCH, HKV, D, generator=gen).to(torch.bfloat16),
+        "slot_mapping": torch.tensor(slots),
+        "block_tables": torch.tensor(tables),
+        "context_lens": torch.tensor(ctx),
     }
+    return {"cache": cache, "ctx": ctx, "width": tables.shape[1], "inputs": inputs}
 
 
-def device_step(w, out, ev_pairs=None):
-    """One step with inputs resident in HBM: per layer, KV write + decode.
-    ``out`` is a list that keeps each layer's output tensor."""
-    from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel as decode
-
-    cache = w["cache"]
-    for layer in range(LAYERS):
-        # The step's slot mapping was validated once when the batch was built.
-        cache.write_slots(w["slots"], w["nk"][layer], w["nv"][layer], layer, validate=False)
-        kc, vc = cache.k_cache[layer], cache.v_cache[layer]
-        if ev_pairs is not None:
-            ev_pairs[layer][0].record()
-        out[layer] = decode(w["q"][layer], kc, vc, w["tables"], w["lens"], BS)
-        if ev_pairs is not None:
-            ev_pairs[layer][1].record()
+def stage(graph, inputs: dict, device_resident: bool) -> None:
+    """Load one step's inputs into a graph's static buffers (device copies
+    for the device-resident measurement, pinned host buffers for e2e)."""
+    for k, v in inputs.items():
+        if device_resident:
+            graph._dev_inputs[k].copy_(v)
+        else:
+            graph.host_inputs[k].copy_(v)
 
 
 def main():
@@ -290,97 +278,85 @@ def main():
     device = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-    from mini_llm_runtime_b200 import _lib
+    from mini_llm_runtime_b200 import PagedDecodeGraph, _lib
 
     _lib.load()
-
     w = build_rank_workload(rank, device)
     nbytes = algorithmic_bytes(w["ctx"])
-    out = [None] * LAYERS
-    w["cache"].validate_slots(w["slots"], w["nk"][0], w["nv"][0], 0)
+    warmup = max(args.warmup, 3)
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
+    def reduce(x: float, op) -> float:
         if world == 1:
             return x
         t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=op)
         return float(t.item())
 
-    def sum_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+    mk = lambda **kw: PagedDecodeGraph(w["cache"], BATCH, w["width"], HQ, range(LAYERS), **kw)  # noqa: E731
 
-    # ---- device-resident timing -------------------------------------------
-    for _ in range(max(args.warmup, 3)):
-        device_step(w, out)
-    ev_pairs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(LAYERS)]
-                for _ in range(args.steps)]
+    # ---- device-resident step: KV write + decode for 24 layers, one graph --
+    g_dev = mk(host_io=False)
+    stage(g_dev, w["inputs"], device_resident=True)
+    g_dev.validate({k: w["inputs"][k] for k in ("context_lens", "block_tables", "slot_mapping")})
+    for _ in range(warmup):
+        g_dev.run(validate=False)
     sampler = ClockSampler(physical_gpu_index(local_rank))
     sampler.start()
     barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
-    for s in range(args.steps):
-        device_step(w, out, ev_pairs[s])
+    for _ in range(args.steps):
+        g_dev.run(validate=False)
     t1.record()
     barrier()
     clocks = sampler.stop()
-    ms_step = max_over_ranks(t0.elapsed_time(t1) / args.steps)
-    dec_ms = [p[0].elapsed_time(p[1]) for step in ev_pairs for p in step]
-    dec_avg_ms = statistics.mean(dec_ms)
-    total_kv = sum_over_ranks(nbytes["kv"] * LAYERS)
-    value = total_kv / (ms_step * 1e-3) / 1e9
-    tokens = sum_over_ranks(BATCH)
+    ms_step = reduce(t0.elapsed_time(t1) / args.steps, dist.ReduceOp.MAX if world > 1 else None)
 
-    # ---- end-to-end through the public API with host buffers ----------------
-    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
-    host = {"q": pin(w["q"]), "nk": pin(w["nk"]), "nv": pin(w["nv"]),
-            "tables": pin(w["tables"]), "lens": pin(w["lens"]), "slots": pin(w["slots"])}
-    host_out = torch.empty((LAYERS, BATCH, HQ, D), dtype=torch.bfloat16).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = host_out.numel() * host_out.element_size()
-    dev_in = {k: torch.empty_like(v, device=device) for k, v in host.items()}
+    # ---- decode kernel alone (roofline): 24 decode launches, one graph -----
+    g_dec = mk(host_io=False, write_kv=False)
+    stage(g_dec, w["inputs"], device_resident=True)
+    for _ in range(warmup):
+        g_dec.run(validate=False)
+    torch.cuda.synchronize()
+    d0 = torch.cuda.Event(enable_timing=True)
+    d1 = torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for _ in range(args.steps):
+        g_dec.run(validate=False)
+    d1.record()
+    torch.cuda.synchronize()
+    dec_ms = d0.elapsed_time(d1) / (args.steps * LAYERS)
 
-    def e2e_step():
-        from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel as decode
-
-        for k in ("tables", "lens", "slots"):
-            dev_in[k].copy_(host[k], non_blocking=True)
-        cache = w["cache"]
-        for layer in range(LAYERS):
-            for k in ("q", "nk", "nv"):
-                dev_in[k][layer].copy_(host[k][layer], non_blocking=True)
-            cache.write_slots(dev_in["slots"], dev_in["nk"][layer], dev_in["nv"][layer], layer,
-                              validate=(layer == 0))
-            o = decode(dev_in["q"][layer], cache.k_cache[layer], cache.v_cache[layer], dev_in["tables"],
-                       dev_in["lens"], BS)
-            host_out[layer].copy_(o, non_blocking=True)
-
-    for _ in range(max(args.warmup, 3)):
-        e2e_step()
+    # ---- end to end: pinned host inputs -> H2D -> step -> D2H, host checks --
+    g_e2e = mk(host_io=True)
+    stage(g_e2e, w["inputs"], device_resident=False)
+    h2d = sum(t.numel() * t.element_size() for t in g_e2e.host_inputs.values())
+    d2h = g_e2e.host_output.numel() * g_e2e.host_output.element_size()
+    for _ in range(warmup):
+        g_e2e.run(validate=True)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        e2e_step()
+        g_e2e.run(validate=True)
     e1.record()
     barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_ms = reduce(e0.elapsed_time(e1) / args.steps, dist.ReduceOp.MAX if world > 1 else None)
+
+    total_kv = reduce(nbytes["kv"] * LAYERS, dist.ReduceOp.SUM if world > 1 else None)
+    tokens = reduce(BATCH, dist.ReduceOp.SUM if world > 1 else None)
+    value = total_kv / (ms_step * 1e-3) / 1e9
     e2e_value = total_kv / (e2e_ms * 1e-3) / 1e9
 
-    # ---- roofline of the decode kernel ------------------------------------
     peak, peak_kind = hbm_peak()
-    achieved = nbytes["decode"] / (dec_avg_ms * 1e-3) / 1e9
+    achieved = nbytes["decode"] / (dec_ms * 1e-3) / 1e9
     traffic = None
     tfile = ROOT / "profiles" / "decode_bf16_config2_traffic.txt"
     if tfile.exists():
@@ -400,7 +376,7 @@ def main():
             "unit": UNIT,
             "n_gpus": world,
             "steps": args.steps,
-            "warmup": max(args.warmup, 3),
+            "warmup": warmup,
             "ms_per_step": ms_step,
             "higher_is_better": True,
             "scaling": "weak",
@@ -413,20 +389,24 @@ def main():
                 "global_batch": BATCH * world,
                 "parallelism": f"request-sharded dp{world}, no communication",
                 "l2": "inputs larger than L2 (1.66 GB of KV streamed per step per GPU), no flush",
+                "launch": "one CUDA graph per step (48 kernel nodes)",
             },
             "tok_per_s": tokens / (ms_step * 1e-3),
             "frac_of_hbm_peak": value / world / peak,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms, "tok_per_s": tokens / (e2e_ms * 1e-3)},
+                    "ms_per_step": e2e_ms, "tok_per_s": tokens / (e2e_ms * 1e-3),
+                    "path": "PagedDecodeGraph.run(): host metadata checks, pinned H2D, 24x(KV write+decode), D2H"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "decode_fast_kernel<bf16,64>",
-                         "bytes_per_launch": nbytes["decode"], "avg_launch_ms": dec_avg_ms},
-            "gpu_launches": args.steps * LAYERS * 2,
+                         "kernel": "decode_flat_kernel<bf16,64>",
+                         "bytes_per_launch": nbytes["decode"], "avg_launch_ms": dec_ms},
+            "gpu_launches": args.steps * g_dev.launches_per_step,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    # Graphs go before the process group.
+    del g_dev, g_dec, g_e2e
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()

@@ -82,21 +82,20 @@ PA_API int pa_kv_scatter(const void* k, int64_t k_s0, int64_t k_s1, int64_t k_s2
                   int num_kv_heads, int head_dim, int pool_dtype, void* stream);
 
 /*
- * Bytes of workspace pa_paged_decode needs for `max_splits` KV partitions
- * per sequence.  The workspace must be zero-filled once when allocated; the
- * kernels leave it ready for the next call (split tickets are reset by the
- * CTA that consumes them).  Calls that share one workspace must be ordered
- * on the same stream.
+ * Bytes of workspace pa_paged_decode needs for exactly these arguments
+ * (0 on invalid arguments).  The workspace holds a status word, the split
+ * tickets and FP32 partial results:
+ *   [0, 256)                         int status (PA_DEVICE_TIMEOUT_* or 0)
+ *   [256, 256 + 4*batch*Hq)          int32 tickets — must read 0 when a call
+ *                                    starts; every call leaves them 0
+ *   [256 + align256(4*batch*Hq), ..) partials (scratch)
+ * Zero the buffer once at allocation; when a later call uses a larger
+ * batch*Hq than earlier calls on the same buffer, re-zero its ticket range
+ * first (it may hold older partials).  Calls sharing a workspace must be
+ * ordered on one stream.
  */
-PA_API size_t pa_decode_workspace_size(int batch, int num_q_heads, int head_dim, int max_splits);
-
-/*
- * Number of KV partitions per sequence pa_paged_decode will use for these
- * arguments (partition_tokens = 0 selects the automatic size).  Lets the
- * caller size the workspace exactly.
- */
-PA_API int pa_decode_num_splits(int batch, int num_kv_heads, int num_q_heads, int head_dim, int block_size,
-                         int64_t bt_width, int partition_tokens, int dtype);
+PA_API size_t pa_decode_workspace_bytes(int batch, int num_kv_heads, int num_q_heads, int head_dim, int block_size,
+                                        int64_t bt_width, int partition_tokens, int dtype);
 
 /*
  * Batched single-token paged decode with split-KV and a log-sum-exp merge.
@@ -118,11 +117,13 @@ PA_API int pa_decode_num_splits(int batch, int num_kv_heads, int num_q_heads, in
  * context_lens : [B] int64, includes the token being decoded (> 0)
  * out          : [B, Hq, D], element strides (o_s0, o_s1)
  * dtype        : F32, F16 or BF16 for q, pools and out (all the same)
- * partition_tokens : KV tokens per split (0 = automatic); rounded up to a
- *                multiple of 16.  A sequence shorter than one partition is
- *                finished in a single CTA without touching the workspace.
- * workspace    : >= pa_decode_workspace_size(B, Hq, D, splits) bytes, zeroed
- *                once at allocation.
+ * partition_tokens : 0 = balanced split chosen by the library (BF16/F16,
+ *                head_dim 64/128: the batch's KV is cut into one equal range
+ *                per SM, ranges that cut a sequence are LSE-merged);
+ *                > 0 = every sequence is cut into partitions of this many
+ *                tokens (rounded up to a multiple of 16), LSE-merged.
+ * workspace    : >= pa_decode_workspace_bytes(...) bytes, 256-byte aligned,
+ *                see pa_decode_workspace_bytes for the zeroing rule.
  */
 PA_API int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_layer,
                     const void* v_pool_layer, int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
@@ -150,13 +151,15 @@ PA_API int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const void
  * block_tables : [num_seqs, bt_width] int64, row stride bt_stride
  * out          : [total_q, Hq, D], element strides (o_s0, o_s1)
  * max_q_len    : upper bound of any chunk length (sizes the launch grid)
+ * status       : optional device int (may be NULL); the tensor-core kernel
+ *                records PA_DEVICE_TIMEOUT_* there if a bounded wait gives up
  */
 PA_API int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
                      const int64_t* context_lens, const int64_t* block_tables, int64_t bt_stride,
                      int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer, int64_t num_blocks,
                      int block_size, int num_kv_heads, int head_dim, void* out, int64_t o_s0, int64_t o_s1,
                      int num_seqs, int64_t total_q, int max_q_len, int num_q_heads, float scale, int dtype,
-                     void* stream);
+                     int* status, void* stream);
 
 /*
  * FP32 P.V accumulator: out[b, d] = sum_n p[b, n] * v[b, n, d] for N = 64,

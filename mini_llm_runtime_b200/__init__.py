@@ -13,9 +13,11 @@ from .paged_attention import (
     paged_attention_prefill_chunk_tiled,
     paged_attention_prefill_varlen,
 )
+from .decode_graph import PagedDecodeGraph
 from .paged_kv_cache import PagedKVCache
 
 __all__ = [
+    "PagedDecodeGraph",
     "PagedKVCache",
     "paged_attention_accumulator_cuda",
     "paged_attention_decode",

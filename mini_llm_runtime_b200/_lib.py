@@ -39,8 +39,7 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p, _i32, _i64,
          _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p],
     ),
-    "pa_decode_workspace_size": (_size, [_i32, _i32, _i32, _i32]),
-    "pa_decode_num_splits": (_i32, [_i32, _i32, _i32, _i32, _i32, _i64, _i32, _i32]),
+    "pa_decode_workspace_bytes": (_size, [_i32, _i32, _i32, _i32, _i32, _i64, _i32, _i32]),
     "pa_paged_decode": (
         _i32,
         [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i64, _i64,
@@ -49,7 +48,7 @@ SIGNATURES: dict[str, tuple] = {
     "pa_chunk_prefill": (
         _i32,
         [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64,
-         _i32, _i32, _i32, _c_void_p, _i64, _i64, _i32, _i64, _i32, _i32, _f32, _i32, _c_void_p],
+         _i32, _i32, _i32, _c_void_p, _i64, _i64, _i32, _i64, _i32, _i32, _f32, _i32, _c_void_p, _c_void_p],
     ),
     "pa_accumulate_pv": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
 }
@@ -118,17 +117,54 @@ def dtype_code(dtype: torch.dtype) -> int:
 
 # ---------------------------------------------------------------------------
 # Decode workspace: one zero-initialised buffer per (device, stream), grown on
-# demand.  The kernels restore their split tickets to zero, so a buffer stays
-# valid across calls; calls on one stream are ordered, so they never overlap.
+# demand.  Layout (csrc/attn_generic.cuh): a 256-byte status word, then the
+# split tickets int32[B * Hq], then the FP32 partials from
+# 256 + align256(4 * B * Hq).  Tickets must read zero when a call starts; the
+# kernels reset every ticket they use, but a later call with a larger B * Hq
+# reaches into bytes an earlier call filled with partials, so those bytes are
+# re-zeroed first.  Calls on one stream are ordered, so they never overlap.
 # ---------------------------------------------------------------------------
-_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+_workspaces: dict[tuple[int, int], "_Workspace"] = {}
+_status_words: dict[int, torch.Tensor] = {}
 
 
-def decode_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+class _Workspace:
+    def __init__(self, device: torch.device, nbytes: int):
+        self.tensor = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        self.clean_end = self.tensor.numel()  # bytes [256, clean_end) hold zeros
+
+
+def _align256(x: int) -> int:
+    return (x + 255) & ~255
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 the kernels set when a bounded wait gives up."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status_words.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _status_words[idx] = t
+    return t
+
+
+def prepare_workspace(ws: "_Workspace", batch: int, num_q_heads: int) -> None:
+    """Make the ticket range of a (batch, Hq) call read zero (see the
+    zeroing rule at pa_decode_workspace_bytes in include/pagedattn.h)."""
+    ticket_end = 256 + 4 * batch * num_q_heads
+    if ticket_end > ws.clean_end:
+        ws.tensor[256:ticket_end].zero_()
+        ws.clean_end = ticket_end
+    else:
+        # This call's partials start at the next 256-byte boundary.
+        ws.clean_end = min(ws.clean_end, 256 + _align256(4 * batch * num_q_heads))
+
+
+def decode_workspace(device: torch.device, nbytes: int, batch: int, num_q_heads: int) -> torch.Tensor:
     key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
     ws = _workspaces.get(key)
-    if ws is None or ws.numel() < nbytes:
-        # Zeroed on the current stream, so it is ready before the next launch.
-        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+    if ws is None or ws.tensor.numel() < nbytes:
+        ws = _Workspace(device, nbytes)  # zeroed on the current stream
         _workspaces[key] = ws
-    return ws
+    prepare_workspace(ws, batch, num_q_heads)
+    return ws.tensor

@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/pagedattn.h"
 
 namespace pa {
@@ -54,11 +56,19 @@ inline int dtype_size(int dt) {
   } while (0)
 
 // ---------------------------------------------------------------------------
-// Bounded waits.  Every spin in these kernels gives up after kSpinLimit
-// polls, records where it stopped in the caller-visible status word and lets
-// the kernel return, so a lost arrival can never hang the GPU.
+// Bounded waits.  Every spin in these kernels gives up after kWaitLimitNs of
+// wall-clock time (%globaltimer), records why in the caller-visible status
+// word and lets the kernel run to its end, so a lost arrival can never hang
+// the GPU.  Legitimate waits (a TMA copy, one tensor-core tile) take
+// microseconds.
 // ---------------------------------------------------------------------------
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint64_t kWaitLimitNs = 500ull * 1000 * 1000;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
@@ -97,10 +107,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Returns false (and records `code`) when the phase never completed.
+// Returns false (and records `code`) when the phase did not complete within
+// kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   record_status(status, code);
   return false;
@@ -120,6 +134,15 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+
+// Programmatic dependent launch.  A kernel launched with the
+// programmatic-stream-serialization attribute may start while the previous
+// kernel in the stream is still running; grid_dep_wait() blocks until that
+// kernel has completed and its memory is visible, so every kernel here calls
+// it before its first global-memory access.  grid_dep_launch() lets the next
+// PDL-launched kernel start early (it still waits for this one to finish).
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -184,12 +207,28 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 EncodeTiledFn get_encode_tiled();
 
-// Encodes a 3-D bf16/f16 map (dims innermost first) with a 128-byte swizzle.
-// Returns PA_OK or PA_ERR_CUDA.
+// Encodes a 3-D bf16/f16 map (dims innermost first).  Returns PA_OK or
+// PA_ERR_CUDA.
 int make_map_3d(CUtensorMap* map, int dtype, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2,
-                CUtensorMapSwizzle swizzle);
+                CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promotion = CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
 
 int num_sms(int device);
+
+// Launch `kern` on `st` with programmatic stream serialization (PDL) enabled.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? PA_OK : PA_ERR_CUDA;
+}
 
 }  // namespace pa

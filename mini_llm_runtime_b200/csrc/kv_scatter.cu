@@ -28,6 +28,8 @@ __global__ void scatter_rows_vec(const uint8_t* __restrict__ k, const uint8_t* _
                                  int64_t v_row_bytes, const void* __restrict__ slots, int64_t num_tokens,
                                  uint8_t* __restrict__ k_pool, uint8_t* __restrict__ v_pool, int64_t num_slots,
                                  int row_chunks) {
+  grid_dep_wait();  // PDL launch: the previous kernel has finished
+  grid_dep_launch();
   const uint8_t* src = blockIdx.y == 0 ? k : v;
   const int64_t src_row = blockIdx.y == 0 ? k_row_bytes : v_row_bytes;
   uint8_t* dst = blockIdx.y == 0 ? k_pool : v_pool;
@@ -54,6 +56,8 @@ __global__ void scatter_rows_cvt(const S* __restrict__ k, int64_t ks0, int64_t k
                                  const S* __restrict__ v, int64_t vs0, int64_t vs1, int64_t vs2,
                                  const void* __restrict__ slots, int64_t num_tokens, Dt* __restrict__ k_pool,
                                  Dt* __restrict__ v_pool, int64_t num_slots, int hkv, int d) {
+  grid_dep_wait();  // PDL launch: the previous kernel has finished
+  grid_dep_launch();
   const int64_t row = static_cast<int64_t>(hkv) * d;
   const int64_t total = num_tokens * row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -81,15 +85,11 @@ int launch_cvt_idx(const void* k, int64_t ks0, int64_t ks1, int64_t ks2, const v
   const int threads = 256;
   int64_t blocks = (total + threads - 1) / threads;
   if (blocks > 148 * 32) blocks = 148 * 32;
-  if (slot64) {
-    scatter_rows_cvt<S, Dt, int64_t><<<(unsigned)blocks, threads, 0, st>>>(
-        (const S*)k, ks0, ks1, ks2, (const S*)v, vs0, vs1, vs2, slots, T, (Dt*)kp, (Dt*)vp, num_slots, hkv, d);
-  } else {
-    scatter_rows_cvt<S, Dt, int32_t><<<(unsigned)blocks, threads, 0, st>>>(
-        (const S*)k, ks0, ks1, ks2, (const S*)v, vs0, vs1, vs2, slots, T, (Dt*)kp, (Dt*)vp, num_slots, hkv, d);
-  }
-  PA_CHECK_LAUNCH();
-  return PA_OK;
+  if (slot64)
+    return launch_pdl(scatter_rows_cvt<S, Dt, int64_t>, dim3((unsigned)blocks), dim3(threads), 0, st, (const S*)k,
+                      ks0, ks1, ks2, (const S*)v, vs0, vs1, vs2, slots, T, (Dt*)kp, (Dt*)vp, num_slots, hkv, d);
+  return launch_pdl(scatter_rows_cvt<S, Dt, int32_t>, dim3((unsigned)blocks), dim3(threads), 0, st, (const S*)k, ks0,
+                    ks1, ks2, (const S*)v, vs0, vs1, vs2, slots, T, (Dt*)kp, (Dt*)vp, num_slots, hkv, d);
 }
 
 template <typename Dt>
@@ -146,17 +146,13 @@ extern "C" int pa_kv_scatter(const void* k, int64_t k_s0, int64_t k_s1, int64_t 
     int64_t blocks = (total + threads - 1) / threads;
     if (blocks > 148 * 16) blocks = 148 * 16;
     dim3 grid(static_cast<unsigned>(blocks), 2);
-    if (slot_is_int64) {
-      scatter_rows_vec<int64_t><<<grid, threads, 0, st>>>(
-          (const uint8_t*)k, (const uint8_t*)v, k_s0 * es, v_s0 * es, slot_mapping, num_tokens,
-          (uint8_t*)k_pool_layer, (uint8_t*)v_pool_layer, num_slots, chunks);
-    } else {
-      scatter_rows_vec<int32_t><<<grid, threads, 0, st>>>(
-          (const uint8_t*)k, (const uint8_t*)v, k_s0 * es, v_s0 * es, slot_mapping, num_tokens,
-          (uint8_t*)k_pool_layer, (uint8_t*)v_pool_layer, num_slots, chunks);
-    }
-    PA_CHECK_LAUNCH();
-    return PA_OK;
+    if (slot_is_int64)
+      return launch_pdl(scatter_rows_vec<int64_t>, grid, dim3(threads), 0, st, (const uint8_t*)k, (const uint8_t*)v,
+                        k_s0 * es, v_s0 * es, slot_mapping, num_tokens, (uint8_t*)k_pool_layer,
+                        (uint8_t*)v_pool_layer, num_slots, chunks);
+    return launch_pdl(scatter_rows_vec<int32_t>, grid, dim3(threads), 0, st, (const uint8_t*)k, (const uint8_t*)v,
+                      k_s0 * es, v_s0 * es, slot_mapping, num_tokens, (uint8_t*)k_pool_layer, (uint8_t*)v_pool_layer,
+                      num_slots, chunks);
   }
   switch (pool_dtype) {
     case PA_DTYPE_F32:

@@ -22,6 +22,7 @@ struct PrefillTcArgs {
   int max_q_len;
   float scale;
   int dtype;
+  int* status;  // device int, may be null; first failed bounded wait is recorded
 };
 
 bool prefill_tc_supported(const PrefillTcArgs& a);

@@ -22,7 +22,7 @@ EncodeTiledFn get_encode_tiled() {
 
 int make_map_3d(CUtensorMap* map, int dtype, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2,
-                CUtensorMapSwizzle swizzle) {
+                CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promotion) {
   EncodeTiledFn enc = get_encode_tiled();
   if (enc == nullptr) return PA_ERR_CUDA;
   CUtensorMapDataType t =
@@ -32,7 +32,7 @@ int make_map_3d(CUtensorMap* map, int dtype, const void* base, uint64_t d0, uint
   cuuint32_t box[3] = {b0, b1, b2};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle, promotion, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? PA_OK : PA_ERR_CUDA;
 }
 

@@ -1,0 +1,176 @@
+"""CUDA-graph capture of a whole decode step of the attention hot path.
+
+A decode step of the reference runs, for every layer, the KV write of the new
+token followed by batched paged decode (model/qwen2.py:608-621, the per-layer
+loop at :1147-1156).  With one Python/ctypes round trip per launch that is
+~50 host launches per step — more host time than the kernels need on a B200.
+``PagedDecodeGraph`` captures the step once (static device buffers, the
+decode workspace and the tensor maps baked into the graph) and replays it
+with a single launch, optionally including the host->device copy of the
+step's inputs from pinned staging buffers and the device->host copy of the
+outputs.
+
+Typical use::
+
+    g = PagedDecodeGraph(cache, batch=64, max_blocks=256, layers=range(24))
+    inp = g.host_inputs          # pinned: q, new_k, new_v, slot_mapping, block_tables, context_lens
+    ... fill inp ...
+    g.run()                      # validate metadata on the host, replay
+    g.synchronize(); out = g.host_output   # [layers, B, Hq, D]
+
+The metadata checks are the ones Qwen2Attention.forward_decode_batch_with_cache
+runs before touching the cache (model/qwen2.py:553-602), done on the pinned
+host copies, so a step never needs a device->host sync.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from . import _lib
+from .paged_kv_cache import PagedKVCache
+
+
+class PagedDecodeGraph:
+    def __init__(
+        self,
+        cache: PagedKVCache,
+        batch: int,
+        max_blocks: int,
+        num_q_heads: int,
+        layers=None,
+        host_io: bool = True,
+        partition_tokens: int = 0,
+        scale: float | None = None,
+        write_kv: bool = True,
+    ):
+        dev = _lib.require_cuda(cache.k_cache, what="PagedDecodeGraph")
+        if cache.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+            raise TypeError("unsupported cache dtype")
+        if num_q_heads % cache.num_kv_heads != 0:
+            raise ValueError("num_query_heads must be divisible by num_kv_heads")
+        self.cache = cache
+        self.device = dev
+        self.batch = batch
+        self.width = max_blocks
+        self.hq = num_q_heads
+        self.layers = list(range(cache.num_layers) if layers is None else layers)
+        self.host_io = host_io
+        self.write_kv = write_kv
+        self.scale = (1.0 / math.sqrt(cache.head_dim)) if scale is None else float(scale)
+        L, B, H, D, HKV = len(self.layers), batch, num_q_heads, cache.head_dim, cache.num_kv_heads
+        dt = cache.dtype
+        self.q = torch.zeros(L, B, H, D, dtype=dt, device=dev)
+        self.new_k = torch.zeros(L, B, HKV, D, dtype=dt, device=dev)
+        self.new_v = torch.zeros(L, B, HKV, D, dtype=dt, device=dev)
+        self.slot_mapping = torch.zeros(B, dtype=torch.long, device=dev)
+        self.block_tables = torch.zeros(B, max_blocks, dtype=torch.long, device=dev)
+        self.context_lens = torch.ones(B, dtype=torch.long, device=dev)
+        self.out = torch.zeros(L, B, H, D, dtype=dt, device=dev)
+        self._dev_inputs = {
+            "q": self.q, "new_k": self.new_k, "new_v": self.new_v, "slot_mapping": self.slot_mapping,
+            "block_tables": self.block_tables, "context_lens": self.context_lens,
+        }
+        self.host_inputs = {k: torch.zeros(v.shape, dtype=v.dtype).pin_memory() for k, v in self._dev_inputs.items()}
+        self.host_output = torch.zeros(self.out.shape, dtype=dt).pin_memory() if host_io else None
+
+        lib = _lib.load()
+        self._lib = lib
+        self._code = _lib.dtype_code(dt)
+        self.partition_tokens = partition_tokens
+        ws_bytes = lib.pa_decode_workspace_bytes(B, HKV, H, D, cache.block_size, max_blocks, partition_tokens,
+                                                 self._code)
+        if ws_bytes == 0:
+            raise ValueError("invalid decode arguments")
+        # Private, zeroed once; every replay leaves the tickets at zero.
+        self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+        self.graph = None
+        self._stream = torch.cuda.Stream(dev)
+        self._capture()
+
+    # -- step body --------------------------------------------------------------
+    def _body(self, stream: int, warm: bool = False) -> None:
+        """Enqueue one step.  ``warm`` = eager first pass before capture: no
+        copies and no KV writes (it must not modify the cache), decode only."""
+        lib, c = self._lib, self.cache
+        B, H, D, HKV, bs = self.batch, self.hq, c.head_dim, c.num_kv_heads, c.block_size
+        if self.host_io and not warm:
+            for k, d in self._dev_inputs.items():
+                d.copy_(self.host_inputs[k], non_blocking=True)
+        num_slots = c.num_blocks * bs
+        for i, layer in enumerate(self.layers):
+            nk, nv, q, o = self.new_k[i], self.new_v[i], self.q[i], self.out[i]
+            kp, vp = c.k_cache[layer], c.v_cache[layer]
+            if self.write_kv and not warm:
+                st = lib.pa_kv_scatter(
+                    nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0), nv.stride(1),
+                    nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(), vp.data_ptr(),
+                    num_slots, HKV, D, self._code, stream)
+                _lib.check(st, "pa_kv_scatter")
+            st = lib.pa_paged_decode(
+                q.data_ptr(), q.stride(0), q.stride(1), kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D,
+                self.block_tables.data_ptr(), self.block_tables.stride(0), self.width, self.context_lens.data_ptr(),
+                o.data_ptr(), o.stride(0), o.stride(1), B, H, self.scale, self._code, self.partition_tokens,
+                self.workspace.data_ptr(), self.workspace.numel(), stream)
+            _lib.check(st, "pa_paged_decode")
+        if self.host_io and not warm:
+            self.host_output.copy_(self.out, non_blocking=True)
+
+    def _capture(self) -> None:
+        # One eager decode-only pass on a side stream (first-use kernel
+        # attributes; length-1 contexts over block 0, nothing written to the
+        # cache), then capture.
+        s = self._stream
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self._body(s.cuda_stream, warm=True)
+        s.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self._body(s.cuda_stream)
+        s.synchronize()
+
+    # -- host-side metadata checks (model/qwen2.py:580-602, paged_kv_cache.py:228-239)
+    def validate(self, inputs: dict | None = None) -> None:
+        src = self.host_inputs if inputs is None else inputs
+        c = self.cache
+        lens = src["context_lens"].numpy()
+        tables = src["block_tables"].numpy()
+        slots = src["slot_mapping"].numpy()
+        if np.any(lens <= 0):
+            raise ValueError("context_lens must be greater than 0")
+        need = (lens + c.block_size - 1) // c.block_size
+        if np.any(need > tables.shape[1]):
+            raise ValueError("block_tables have insufficient blocks for context_lens")
+        used = np.arange(tables.shape[1])[None, :] < need[:, None]
+        if np.any(used & ((tables < 0) | (tables >= c.num_blocks))):
+            raise ValueError("block_tables contain an invalid physical block")
+        pos = lens - 1
+        expected = tables[np.arange(len(lens)), pos // c.block_size] * c.block_size + pos % c.block_size
+        if np.any(slots != expected):
+            raise ValueError("slot_mapping must match block_tables and positions")
+        if np.unique(slots).size != slots.size:
+            raise ValueError("decode requests must use distinct write slots")
+
+    def run(self, validate: bool = True) -> None:
+        """Validate the staged metadata on the host and replay the step on the
+        current stream (asynchronous)."""
+        if validate:
+            self.validate(self.host_inputs if self.host_io else {
+                k: v.cpu() for k, v in self._dev_inputs.items() if k in ("context_lens", "block_tables", "slot_mapping")})
+        cur = torch.cuda.current_stream(self.device)
+        self._stream.wait_stream(cur)
+        with torch.cuda.stream(self._stream):
+            self.graph.replay()
+        cur.wait_stream(self._stream)
+
+    def synchronize(self) -> None:
+        torch.cuda.current_stream(self.device).synchronize()
+
+    @property
+    def launches_per_step(self) -> int:
+        """Kernels of this library launched per replay."""
+        return (2 if self.write_kv else 1) * len(self.layers)

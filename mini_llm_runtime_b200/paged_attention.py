@@ -77,10 +77,10 @@ def _decode_launch(
     seq_lens = seq_lens.contiguous()
     code = _lib.dtype_code(q.dtype)
     width = block_tables.shape[1]
-    splits = lib.pa_decode_num_splits(b, hkv, hq, d, bs, width, partition_tokens, code)
-    _lib.check(splits if splits < 0 else 0, "pa_decode_num_splits")
-    ws_bytes = lib.pa_decode_workspace_size(b, hq, d, splits)
-    ws = _lib.decode_workspace(dev, ws_bytes)
+    ws_bytes = lib.pa_decode_workspace_bytes(b, hkv, hq, d, bs, width, partition_tokens, code)
+    if ws_bytes == 0:
+        raise ValueError("invalid decode arguments")
+    ws = _lib.decode_workspace(dev, ws_bytes, b, hq)
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     with torch.cuda.device(dev):
@@ -250,7 +250,7 @@ def _prefill_launch(
             context_lens.contiguous().data_ptr(), block_tables.data_ptr(), block_tables.stride(0),
             block_tables.shape[1], k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d,
             out.data_ptr(), out.stride(0), out.stride(1), cu_q_lens.shape[0] - 1, total_q, int(max_q_len), hq,
-            float(scale), _lib.dtype_code(q.dtype), _lib.stream_handle(dev),
+            float(scale), _lib.dtype_code(q.dtype), _lib.status_word(dev).data_ptr(), _lib.stream_handle(dev),
         )
     _lib.check(st, "pa_chunk_prefill")
     return out

@@ -41,23 +41,19 @@ def test_status_strings_and_version():
     assert lib.pa_status_string(12345) == b"unknown status"
 
 
-def test_workspace_size_grows_with_splits():
+def test_workspace_bytes():
     lib = _lib.load()
-    a = lib.pa_decode_workspace_size(64, 14, 64, 1)
-    b = lib.pa_decode_workspace_size(64, 14, 64, 16)
-    assert 0 < a < b
-    assert b >= 64 * 14 * 16 * (64 + 2) * 4
-    assert lib.pa_decode_workspace_size(0, 14, 64, 1) == 0
-
-
-def test_num_splits_honours_partition_size():
-    lib = _lib.load()
-    # Config 3: 32768-token contexts, 16 partitions of 2048 tokens.
-    assert lib.pa_decode_num_splits(8, 2, 14, 64, 16, 2048, 2048, 2) == 16
-    assert lib.pa_decode_num_splits(8, 2, 14, 64, 16, 2048, 4096, 2) == 8
-    # FP32 goes to the CUDA-core kernel (partitions in multiples of 256).
-    assert lib.pa_decode_num_splits(8, 2, 14, 64, 16, 2048, 2048, 0) == 16
-    assert lib.pa_decode_num_splits(4, 3, 14, 64, 16, 10, 0, 2) < 0  # Hq % Hkv != 0
+    # Balanced kernel (BF16, D 64): status + tickets + per-CTA partials.
+    a = lib.pa_decode_workspace_bytes(64, 2, 14, 64, 16, 256, 0, 2)
+    assert a >= 256 + 64 * 14 * 4
+    # Explicit partitions (config 3: 16 partitions of 2048 tokens).
+    b = lib.pa_decode_workspace_bytes(8, 2, 14, 64, 16, 2048, 2048, 2)
+    assert b >= 256 + 8 * 14 * 16 * (64 + 2) * 4
+    # FP32 uses the CUDA-core kernel (partitions in multiples of 256 tokens).
+    c = lib.pa_decode_workspace_bytes(8, 2, 14, 64, 16, 2048, 2048, 0)
+    assert c >= 256 + 8 * 14 * 16 * (64 + 2) * 4
+    assert lib.pa_decode_workspace_bytes(0, 2, 14, 64, 16, 256, 0, 2) == 0
+    assert lib.pa_decode_workspace_bytes(4, 3, 14, 64, 16, 10, 0, 2) == 0  # Hq % Hkv != 0
 
 
 @pytest.mark.parametrize(
@@ -71,7 +67,7 @@ def test_num_splits_honours_partition_size():
                                     4, 14, 1.0, 2, 0, None, 0, None),
         lambda L: L.pa_kv_scatter(None, 0, 0, 0, None, 0, 0, 0, 0, None, 1, 4, None, None, 64, 2, 64, 0, None),
         lambda L: L.pa_chunk_prefill(None, 0, 0, None, None, None, 0, 1, None, None, 1, 16, 2, 64, None, 0, 0,
-                                     1, 4, 4, 14, 1.0, 2, None),
+                                     1, 4, 4, 14, 1.0, 2, None, None),
         lambda L: L.pa_accumulate_pv(None, None, None, 3, None),
     ],
 )

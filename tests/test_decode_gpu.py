@@ -86,7 +86,8 @@ def test_golden_bf16_against_fp32_reference(cuda_device):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("hq,hkv", [(14, 2), (4, 4), (8, 1), (28, 4), (32, 8)], ids=["gqa7", "mha", "mqa", "gqa7x4", "gqa4"])
+@pytest.mark.parametrize("hq,hkv", [(14, 2), (4, 4), (8, 1), (28, 4), (32, 8), (40, 2)],
+                         ids=["gqa7", "mha", "mqa", "gqa7x4", "gqa4", "gqa20"])
 @pytest.mark.parametrize("d", [64, 128])
 def test_decode_geometries(cuda_device, dtype, hq, hkv, d):
     ctx = [1, 15, 16, 17, 63, 64, 65, 127, 128, 255, 513, 700]
@@ -180,3 +181,67 @@ def test_decode_is_deterministic_and_does_not_write_pools(cuda_device):
     assert torch.equal(a, b)
     assert torch.equal(k0.view(torch.int16), case["k"].view(torch.int16))
     assert torch.equal(v0.view(torch.int16), case["v"].view(torch.int16))
+
+
+def test_workspace_reuse_across_batch_sizes(cuda_device):
+    """Calls with growing batch on one stream share the cached workspace; the
+    ticket range of the larger call must not see the smaller call's partials."""
+    for i, ctx in enumerate([[700, 3000], [4000] * 16, [100, 5000, 33], [2500] * 64]):
+        case = make_decode_case(ctx, 14, 2, 64, 16, torch.bfloat16, cuda_device, seed=50 + i)
+        for part in (0, 256):
+            out = paged_attention_decode_split_kv(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16,
+                                                  partition_size=part) if part else \
+                paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+            check(out, oracle_decode(case), torch.bfloat16)
+
+
+def test_tiny_batches_leave_ctas_idle(cuda_device):
+    """Fewer KV sub-blocks than CTAs: most CTAs get an empty range and one
+    sequence spans many single-sub-block CTAs."""
+    for ctx in ([1], [160], [16 * 40 + 3], [5, 7, 300]):
+        case = make_decode_case(ctx, 8, 1, 128, 16, torch.float16, cuda_device, seed=len(ctx) + ctx[0])
+        out = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+        check(out, oracle_decode(case), torch.float16)
+
+
+def test_decode_graph_step_matches_eager(cuda_device):
+    """PagedDecodeGraph (CUDA graph of KV write + decode per layer, with
+    pinned host I/O) gives the same cache and outputs as eager calls."""
+    from mini_llm_runtime_b200 import PagedDecodeGraph
+
+    torch.manual_seed(3)
+    ctx = [37, 600, 1025, 64]
+    layers, hq, hkv, d, bs = 3, 14, 2, 64, 16
+    need = [(c + bs - 1) // bs for c in ctx]
+    nb = sum(need) + 5
+    perm = torch.randperm(nb).tolist()
+    tables, cur = [], 0
+    for n in need:
+        tables.append(perm[cur:cur + n] + [-1] * (max(need) - n))
+        cur += n
+    cache = PagedKVCache(layers, nb, bs, hkv, d, dtype=torch.bfloat16, device=cuda_device)
+    cache.k_cache.normal_()
+    cache.v_cache.normal_()
+    ref = PagedKVCache(layers, nb, bs, hkv, d, dtype=torch.bfloat16, device=cuda_device)
+    ref.k_cache.copy_(cache.k_cache)
+    ref.v_cache.copy_(cache.v_cache)
+    g = PagedDecodeGraph(cache, batch=len(ctx), max_blocks=max(need), num_q_heads=hq, layers=range(layers))
+    hi = g.host_inputs
+    hi["q"].copy_(torch.randn(hi["q"].shape).to(torch.bfloat16))
+    hi["new_k"].copy_(torch.randn(hi["new_k"].shape).to(torch.bfloat16))
+    hi["new_v"].copy_(torch.randn(hi["new_v"].shape).to(torch.bfloat16))
+    hi["block_tables"].copy_(torch.tensor(tables))
+    hi["context_lens"].copy_(torch.tensor(ctx))
+    hi["slot_mapping"].copy_(torch.tensor([tables[b][(c - 1) // bs] * bs + (c - 1) % bs for b, c in enumerate(ctx)]))
+    g.run()
+    g.synchronize()
+    dv = {k: v.to(cuda_device) for k, v in hi.items()}
+    for layer in range(layers):
+        ref.write_slots(dv["slot_mapping"], dv["new_k"][layer], dv["new_v"][layer], layer)
+        exp = paged_attention_decode_batch_parallel(dv["q"][layer], ref.k_cache[layer], ref.v_cache[layer],
+                                                    dv["block_tables"], dv["context_lens"], bs)
+        assert torch.equal(g.host_output[layer], exp.cpu())
+    assert torch.equal(cache.k_cache.view(torch.int16), ref.k_cache.view(torch.int16))
+    with pytest.raises(ValueError, match="slot_mapping must match"):
+        hi["slot_mapping"][0] += 1
+        g.run()
