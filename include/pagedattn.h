@@ -132,6 +132,27 @@ PA_API int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const void
                     int partition_tokens, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * pa_paged_decode without a caller-supplied workspace: for callers that
+ * cannot allocate device memory (a host runtime that owns every device byte
+ * through its own arena, an FFI host with no device allocator, a serving
+ * loop that must not let cudaMalloc synchronise the device).  No counterpart
+ * in the reference: its decode is PyTorch code that allocates freely.
+ *
+ * The scratch is a fixed 16 MiB array inside the library (held on every GPU
+ * that loads it until exit); calls whose pa_decode_workspace_bytes(...)
+ * exceeds 16 MiB return PA_ERR_CAPACITY.  The first call on a device looks
+ * the array's address up with cudaGetSymbolAddress, so make it before any
+ * stream capture.  Every call clears the scratch's status word and tickets
+ * on `stream` and then shares the array: calls that overlap on the GPU race.
+ * Arguments and results are those of pa_paged_decode.  Allocates nothing.
+ */
+PA_API int pa_paged_decode_noalloc(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_layer,
+                                   const void* v_pool_layer, int64_t num_blocks, int block_size, int num_kv_heads,
+                                   int head_dim, const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
+                                   const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
+                                   int num_q_heads, float scale, int dtype, int partition_tokens, void* stream);
+
+/*
  * Causal chunk-prefill over a paged cache, batched over sequences.
  *
  * Sequence s owns packed query rows [cu_q_lens[s], cu_q_lens[s+1]) of q; its
