@@ -545,7 +545,8 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
       const int64_t base = rec(r);
       float2 ml = make_float2(-INFINITY, 0.f);
       if (base >= 0) ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (base + h) * 2));
-      if (nm < 4) mine[nm++] = ml;
+      if (nm < 4) mine[nm] = ml;
+      ++nm;
       mx = fmaxf(mx, ml.x);
     }
 #pragma unroll
@@ -572,6 +573,8 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
   }
   __syncthreads();
   // Phase 2: items (row, 8 columns) x stripes of records, reduced in smem.
+  // Records are taken four at a time with every load issued before any is
+  // used, so a stripe of records costs one memory round trip.
   const int items = hn * (D / 8);
   const int stripes = kCombineThreads / items;
   const int item = tid % items, stripe = tid / items;
@@ -579,23 +582,34 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
   if (stripe < stripes) {
     const int h = item / (D / 8), d = 8 * (item - h * (D / 8));
     const float mx = smx[h];
-#pragma unroll 2
-    for (int r = stripe; r < nrec; r += stripes) {
-      const int64_t base = rec(r);
-      if (base < 0) continue;
-      const float m = __ldcg(p.part_ml + (base + h) * 2);
-      if (m == -INFINITY) continue;
-      const float wt = exp2f(m - mx);
-      const float4* src = reinterpret_cast<const float4*>(p.part_o + (base + h) * D + d);
-      const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
-      acc[0] = fmaf(wt, v0.x, acc[0]);
-      acc[1] = fmaf(wt, v0.y, acc[1]);
-      acc[2] = fmaf(wt, v0.z, acc[2]);
-      acc[3] = fmaf(wt, v0.w, acc[3]);
-      acc[4] = fmaf(wt, v1.x, acc[4]);
-      acc[5] = fmaf(wt, v1.y, acc[5]);
-      acc[6] = fmaf(wt, v1.z, acc[6]);
-      acc[7] = fmaf(wt, v1.w, acc[7]);
+    for (int r0 = stripe; r0 < nrec; r0 += 4 * stripes) {
+      float m[4];
+      float4 v0[4], v1[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = r0 + u * stripes;
+        const int64_t base = r < nrec ? rec(r) : -1;
+        m[u] = -INFINITY;
+        v0[u] = v1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (base >= 0) {
+          m[u] = __ldcg(p.part_ml + (base + h) * 2);
+          const float4* src = reinterpret_cast<const float4*>(p.part_o + (base + h) * D + d);
+          v0[u] = __ldcg(src);
+          v1[u] = __ldcg(src + 1);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float wt = m[u] == -INFINITY ? 0.f : exp2f(m[u] - mx);
+        acc[0] = fmaf(wt, v0[u].x, acc[0]);
+        acc[1] = fmaf(wt, v0[u].y, acc[1]);
+        acc[2] = fmaf(wt, v0[u].z, acc[2]);
+        acc[3] = fmaf(wt, v0[u].w, acc[3]);
+        acc[4] = fmaf(wt, v1[u].x, acc[4]);
+        acc[5] = fmaf(wt, v1[u].y, acc[5]);
+        acc[6] = fmaf(wt, v1[u].z, acc[6]);
+        acc[7] = fmaf(wt, v1[u].w, acc[7]);
+      }
     }
   }
 #pragma unroll
