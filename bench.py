@@ -60,6 +60,10 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--kernel", choices=sorted(KERNEL_CASES), default=None,
+                    help="time one kernel case alone (secondary configs; the small ncu targets)")
+    ap.add_argument("--layers", type=int, default=None, help="layers the --kernel case rotates over")
+    ap.add_argument("--reps", type=int, default=None, help="graph replays timed by the --kernel case")
     return ap.parse_args()
 
 
@@ -67,14 +71,26 @@ def env_rank():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
-def hbm_peak():
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def _peak(key: str, fallback: float):
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+            return float(json.loads(p.read_text())[key]), "measured"
         except (KeyError, ValueError):
             pass
-    return FALLBACK_HBM_GBS, "fallback"
+    return fallback, "fallback"
+
+
+def hbm_peak():
+    return _peak("hbm_gbs", FALLBACK_HBM_GBS)
+
+
+def bf16_peak():
+    """Burst BF16 peak: the kernel cases are timed alone, a few ms at a time."""
+    return _peak("bf16_tflops", FALLBACK_BF16_TFLOPS)
 
 
 def make_metadata(seed: int):
@@ -163,6 +179,161 @@ def physical_gpu_index(local_rank: int) -> int:
         if local_rank < len(ids) and ids[local_rank].isdigit():
             return int(ids[local_rank])
     return local_rank
+
+
+# ---------------------------------------------------------------------------
+# Single-kernel cases: BASELINE configs 3, 4 and the two halves of config 5,
+# and one layer of config 2.  Each case builds `layers` independent layers
+# (pools, queries) so consecutive launches stream different memory, captures
+# one launch per layer into a CUDA graph and times graph replays.
+# ---------------------------------------------------------------------------
+
+
+def _random_tables(rng, ctx: np.ndarray, bs: int, slack: float = 1.1):
+    """Block tables from a random permutation of a pool of total blocks x
+    slack, padded with -1 (benchmarks/benchmark_paged_attention.py:449-456)."""
+    need = (ctx + bs - 1) // bs
+    nb = int(math.ceil(need.sum() * slack))
+    perm = rng.permutation(nb)
+    tables = np.full((len(ctx), int(need.max())), -1, dtype=np.int64)
+    cur = 0
+    for b in range(len(ctx)):
+        tables[b, : need[b]] = perm[cur : cur + need[b]]
+        cur += need[b]
+    return tables, nb
+
+
+def _bf16_randn(shape, device, gen):
+    return torch.randn(shape, device=device, generator=gen).to(torch.bfloat16)
+
+
+def _decode_case(device, layers, ctx, hq, hkv, d, partition, seed):
+    from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel, paged_attention_decode_split_kv
+
+    rng = np.random.default_rng(seed)
+    tables, nb = _random_tables(rng, ctx, BS)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    k = _bf16_randn((layers, nb, BS, hkv, d), device, gen)
+    v = _bf16_randn((layers, nb, BS, hkv, d), device, gen)
+    q = _bf16_randn((layers, len(ctx), hq, d), device, gen)
+    bt, cl = torch.tensor(tables, device=device), torch.tensor(ctx, device=device)
+    if partition:
+        fn = lambda l: paged_attention_decode_split_kv(q[l], k[l], v[l], bt, cl, BS, partition)  # noqa: E731
+    else:
+        fn = lambda l: paged_attention_decode_batch_parallel(q[l], k[l], v[l], bt, cl, BS)  # noqa: E731
+    work = int(ctx.sum()) * hkv * d * 2 * 2 + 2 * len(ctx) * hq * d * 2 + int(((ctx + BS - 1) // BS).sum()) * 8
+    return fn, work
+
+
+def _prefill_case(device, layers, prefix, chunk, hq, hkv, d, seed):
+    from mini_llm_runtime_b200 import paged_attention_prefill_varlen
+
+    rng = np.random.default_rng(seed)
+    ctx = prefix + chunk
+    tables, nb = _random_tables(rng, ctx, BS)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    k = _bf16_randn((layers, nb, BS, hkv, d), device, gen)
+    v = _bf16_randn((layers, nb, BS, hkv, d), device, gen)
+    q = _bf16_randn((layers, int(chunk.sum()), hq, d), device, gen)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(chunk)]), device=device)
+    bt, cl = torch.tensor(tables, device=device), torch.tensor(ctx, device=device)
+    cmax = int(chunk.max())
+    fn = lambda l: paged_attention_prefill_varlen(q[l], cu, cl, bt, k[l], v[l], cmax)  # noqa: E731
+    return fn, prefill_flops(prefix, chunk, hq, d)
+
+
+def prefill_flops(prefix: np.ndarray, chunk: np.ndarray, hq: int, d: int) -> int:
+    """Unmasked causal FLOPs: QK^T and PV each cost 2*D per (query, key)
+    pair, over the keys at or before each query's absolute position."""
+    pairs = sum(int(c) * (int(p) + 1) + int(c) * (int(c) - 1) // 2 for p, c in zip(prefix, chunk))
+    return 4 * d * hq * pairs
+
+
+def _case_config2(device, layers):
+    ctx = make_metadata(1000)[0]
+    return _decode_case(device, layers, ctx, HQ, HKV, D, 0, 11)
+
+
+def _case_config3(device, layers):
+    ctx = np.full(8, 32768, dtype=np.int64)
+    return _decode_case(device, layers, ctx, HQ, HKV, D, 32768 // 16, 13)
+
+
+def _case_config4(device, layers):
+    rng = np.random.default_rng(4)
+    prefix = rng.integers(0, 2049, size=16).astype(np.int64)
+    return _prefill_case(device, layers, prefix, np.full(16, 512, dtype=np.int64), HQ, HKV, D, 14)
+
+
+def _case_config5_decode(device, layers):
+    ctx = np.random.default_rng(5).integers(256, 8193, size=256).astype(np.int64)
+    return _decode_case(device, layers, ctx, 28, 4, 128, 0, 15)
+
+
+def _case_config5_prefill(device, layers):
+    prefix = np.random.default_rng(6).integers(0, 4097, size=4).astype(np.int64)
+    return _prefill_case(device, layers, prefix, np.full(4, 1024, dtype=np.int64), 28, 4, 128, 16)
+
+
+# name -> (builder, bound, default layers, description)
+KERNEL_CASES = {
+    "decode-config2": (_case_config2, "hbm", 8,
+                       "config2 one layer: bf16 batched decode, B64, 14/2, D64, ctx U[128,4096]"),
+    "split-config3": (_case_config3, "hbm", 4,
+                      "config3: bf16 split-KV decode, B8 x 32768, 14/2, D64, 16 partitions of 2048"),
+    "prefill-config4": (_case_config4, "tensor", 4,
+                        "config4: bf16 causal chunk-prefill, 16 seqs x 512 on prefix U[0,2048], 14/2, D64"),
+    "decode-config5": (_case_config5_decode, "hbm", 2,
+                       "config5 decode half: bf16 batched decode, B256, 28/4, D128, ctx U[256,8192]"),
+    "prefill-config5": (_case_config5_prefill, "tensor", 4,
+                        "config5 prefill half: bf16 chunk-prefill, 4 x 1024 on prefix U[0,4096], 28/4, D128"),
+}
+
+
+def time_kernel_case(name: str, device, layers: int | None = None, reps: int | None = None,
+                     warmup: int = 3) -> dict:
+    """Device time per launch of one kernel case (CUDA events around graph
+    replays on the current stream) and its roofline figures."""
+    build, bound, default_layers, desc = KERNEL_CASES[name]
+    layers = layers or default_layers
+    reps = reps or max(1, 64 // layers)
+    fn, work = build(device, layers)
+    for l in range(layers):
+        fn(l)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for l in range(layers):
+            fn(l)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * layers)
+    del graph
+    if bound == "hbm":
+        peak, src = hbm_peak()
+        achieved, unit = work / (ms * 1e-3) / 1e9, "GB/s"
+    else:
+        peak, src = bf16_peak()
+        achieved, unit = work / (ms * 1e-3) / 1e12, "TFLOP/s"
+    return {"case": name, "workload": desc, "bound": bound, "us_per_launch": ms * 1e3,
+            "work_per_launch": work, "work_unit": "bytes" if bound == "hbm" else "flops",
+            "achieved": achieved, "unit": unit, "peak": peak, "peak_source": src, "frac": achieved / peak,
+            "layers": layers, "reps": reps}
+
+
+def run_kernel_case(args):
+    rank, world, local_rank = env_rank()
+    torch.cuda.set_device(local_rank)
+    r = time_kernel_case(args.kernel, torch.device("cuda", local_rank), args.layers, args.reps, max(args.warmup, 1))
+    if rank == 0:
+        print(json.dumps(r), flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -271,6 +442,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
+    if args.kernel:
+        run_kernel_case(args)
+        return
 
     import torch.distributed as dist
 
@@ -364,6 +538,14 @@ def main():
             if line.startswith("dram_bytes_per_launch:"):
                 traffic = float(line.split(":", 1)[1])
 
+    # ---- secondary configs, one kernel at a time (same GPU, after the step) --
+    secondary = {}
+    if world == 1:
+        for name in ("split-config3", "prefill-config4", "decode-config5", "prefill-config5"):
+            r = time_kernel_case(name, device)
+            secondary[name] = {k: r[k] for k in ("workload", "us_per_launch", "achieved", "unit", "frac")}
+            torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_reference_sample(steps=5, warmup=1)
@@ -400,6 +582,7 @@ def main():
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "kernel": "decode_flat_kernel<bf16,64>",
                          "bytes_per_launch": nbytes["decode"], "avg_launch_ms": dec_ms},
+            "secondary": secondary,
             "gpu_launches": args.steps * g_dev.launches_per_step,
             "clocks": clocks,
             "cpu_baseline": cpu,

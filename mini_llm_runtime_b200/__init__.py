@@ -15,10 +15,12 @@ from .paged_attention import (
 )
 from .decode_graph import PagedDecodeGraph
 from .paged_kv_cache import PagedKVCache
+from .qwen2_attention import Qwen2Attention
 
 __all__ = [
     "PagedDecodeGraph",
     "PagedKVCache",
+    "Qwen2Attention",
     "paged_attention_accumulator_cuda",
     "paged_attention_decode",
     "paged_attention_decode_batch_parallel",
