@@ -1,36 +1,44 @@
-// tcgen05 causal chunk-prefill over a paged KV cache (BF16/F16, head_dim 64).
+// tcgen05 causal chunk-prefill over a paged KV cache (BF16/F16, head_dim 64
+// or 128).
 //
 // Math: for every query row of a chunk, softmax(scale * q K^T) V over the
 // keys at absolute positions <= prefix + i (reference:
 // kernels/reference/paged_attention.py:346-434 — the tiled online softmax
 // of :398-431 — and its dense twin :282-343).
 //
-// Work unit (one CTA): (sequence, KV head, M-tile).  The M-tile packs the
-// whole GQA group into the 128 MMA rows: row r = (query position r / G,
-// query head r % G), P = floor(128 / G) positions per tile (18 for Qwen2.5's
-// group of 7 -> 126 live rows), so every K/V tile loaded from the paged pool
-// feeds all G query heads at once.  Tiles with the largest query positions
-// (most KV tiles) launch first.
+// Work item: (sequence, KV head, pair of M-tiles).  An M-tile packs the GQA
+// group into the 128 MMA rows: row r = (query position r / G, query head
+// r % G), P = floor(128 / G) positions per tile (18 for a group of 7 -> 126
+// live rows), so every K/V tile staged from the paged pool feeds all G query
+// heads of both M-tiles.  The kernel is persistent (one CTA per SM); CTA b
+// takes items b, b + grid, ... of a list ordered by descending query
+// position, so the longest items start first.  All roles walk the same list.
 //
-// Warp roles (192 threads, one CTA per SM):
-//   warp 0      TMA producer: Q tile once (3-D box {64, G, P} straight from
-//               the packed [T, Hq, D] tensor), then per 128-token KV tile 8+8
-//               boxes {64, 1, 16} addressed through the block table into a
-//               2-stage ring (128-byte swizzle, canonical UMMA K-major
-//               layout).  Blocks past the context use an out-of-range
-//               coordinate, which TMA fills with zeros.
-//   warp 1      TMEM owner + single-thread MMA issuer:
-//                 S_j = Q K_j^T   (M128 N128 K64, both K-major)  -> TMEM S[j%2]
-//                 O_j = P_j V_j   (M128 N64 K128, V as MN-major B) -> TMEM O[j%2]
-//               S_{j+1} is issued before O_j so QK^T of the next tile overlaps
-//               the softmax of this one.
-//   warps 2..5  softmax: one thread per row (TMEM lane), FP32 online softmax
-//               in the log2 domain, causal mask only on diagonal tiles,
-//               P written to shared memory as BF16/F16 (SW128 K-major),
-//               O tile read back from TMEM and accumulated in registers with
-//               the running rescale, final 1/l and store.
-// Every mbarrier wait is bounded (status word + early exit); TMEM is freed
-// on every path.
+// Warp roles (384 threads; setmaxnreg moves registers to the softmax):
+//   warp 8      TMA producer: the item's two Q tiles (3-D boxes {64, G, P}
+//               straight from the packed [T, Hq, D] tensor, double-buffered
+//               across items when shared memory allows), then per KV tile
+//               of N tokens 8 K boxes + 8 V boxes {64, 1, 16} addressed
+//               through the block table into a ring of stages (128-byte
+//               swizzle = canonical UMMA layout).  Tokens at or past the
+//               context use an out-of-range coordinate: TMA fills zeros.
+//   warp 9      TMEM owner + single-thread MMA issuer.  Per KV tile j and
+//               M-tile w:  O_w += P_w(j-1) V(j-1)  then  S_w(j) = Q_w K(j)^T.
+//               A commit after S_w(j) therefore also covers the preceding
+//               P V, which is what lets the softmax warps rescale O_w in
+//               TMEM as soon as S_w(j) is ready.
+//   warps 0-3   softmax of M-tile 0, warps 4-7 softmax of M-tile 1 (one row
+//               per thread, FP32 statistics in the log2 domain).  While one
+//               group exponentiates, the tensor core works for the other.
+//               O stays in TMEM for the whole item; it is rescaled only when
+//               a row's running maximum grows by more than 2^8 (the
+//               unnormalised P then stays below 256, exact enough in FP32 and
+//               BF16), and read once at the end for 1/l and the store.
+//   warps 10-11 idle.
+// Every mbarrier wait is bounded; a failed wait records a status code, sets
+// a CTA-wide abort flag, and every role winds down (in-flight copies and
+// MMAs are drained, TMEM is freed) without further waiting.
+#include <algorithm>
 #include <type_traits>
 
 #include "prefill_tc.cuh"
@@ -39,301 +47,439 @@
 namespace pa {
 namespace {
 
-constexpr int kM = 128;      // MMA rows (packed query positions x heads)
-constexpr int kN = 128;      // KV tokens per tile
-constexpr int kD = 64;       // head_dim
-constexpr int kStages = 2;   // K/V ring depth
-constexpr int kThreads = 192;
-constexpr int kTileBytes = kN * kD * 2;  // 16 KB: one K, V or Q tile
-constexpr int kPBytes = kM * kN * 2;     // 32 KB: one P tile
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;
-constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffP = kOffV + kStages * kTileBytes;
-constexpr int kOffBar = kOffP + 2 * kPBytes;
-constexpr int kNumBars = 1 + 2 * kStages + 8 + 1;
-constexpr int kOffTmem = kOffBar + kNumBars * 8;
-constexpr size_t kSmem = 1024 + kOffTmem + 16;
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
-constexpr uint32_t kTmemS = 0, kTmemO = 256;
+constexpr int kM = 128;                      // MMA rows per M-tile
+constexpr int kThreads = 384;                // 3 warpgroups
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+// setmaxnreg budgets (per thread): launch gives 168 x 384; the control
+// warpgroup drops to 64 so the two softmax warpgroups can hold a 128-float
+// S row: 4*32*64 + 8*32*216 <= 384*168.
+constexpr int kCtrlRegs = 64, kSoftmaxRegs = 216;
+constexpr float kRescaleLog2 = 8.f;          // lazy-rescale threshold (log2 units)
+constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
+
+template <int D> struct Shape;
+// N = KV tokens per tile, ST = K/V ring stages, QB = Q buffers (items in flight).
+template <> struct Shape<64> { static constexpr int N = 128, ST = 3, QB = 2; };
+template <> struct Shape<128> { static constexpr int N = 64, ST = 3, QB = 1; };
+
+template <int D>
+struct Lay {
+  static constexpr int N = Shape<D>::N, ST = Shape<D>::ST, QB = Shape<D>::QB;
+  static constexpr int kDH = D / 64;           // 128-byte column slabs per row
+  static constexpr int kSlab = kM * 128;       // one 128-row slab (16 KB)
+  static constexpr int kQTile = kDH * kSlab;   // Q tile: [kDH][128 rows][128 B]
+  static constexpr int kKVTile = kDH * N * 128;  // K or V tile: [kDH][N rows][128 B]
+  static constexpr int kPTile = (N / 64) * kSlab;  // P tile: [N/64][128 rows][128 B]
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + QB * 2 * kQTile;
+  static constexpr int kOffV = kOffK + ST * kKVTile;
+  static constexpr int kOffP = kOffV + ST * kKVTile;
+  static constexpr int kOffBar = kOffP + 2 * kPTile;
+  static constexpr int kNumBars = 2 * QB + 2 * ST + 8 + 1;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr size_t kSmem = 1024 + kOffMisc + 16;
+  static constexpr uint32_t kTmemS = 0;        // S_w at columns [w N, (w+1) N)
+  static constexpr uint32_t kTmemO = 2 * N;    // O_w at columns [2N + w D, 2N + (w+1) D)
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kBoxes = (N / kBoxTokens) * kDH;  // per K (and per V) tile
+  static_assert(kBoxes <= 32, "one TMA box per producer lane");
+  static_assert(kTmemO + 2 * D <= kTmemCols, "TMEM budget");
+};
 
 struct TcParams {
   const int64_t* cu_q;
   const int64_t* context_lens;
   const int64_t* bt;
   int64_t bt_stride, bt_width;
-  int64_t num_slots;
+  int64_t num_blocks, num_slots;
   void* out;
   int64_t o_s0, o_s1;
-  int G, P, bs, mtiles;
+  int64_t ctx_cap;  // min(bt_width * bs, 2^31 - 1)
+  int64_t total_q;
+  int G, P, bs, Hkv, num_seqs, pairs, num_items;
   float scale_log2;
   int* status;
 };
 
-template <typename T> struct Pack2;
-template <> struct Pack2<__nv_bfloat16> {
-  __device__ __forceinline__ static uint32_t run(float a, float b) { return MmaOp<__nv_bfloat16>::pack(a, b); }
-};
-template <> struct Pack2<__half> {
-  __device__ __forceinline__ static uint32_t run(float a, float b) { return MmaOp<__half>::pack(a, b); }
+// Positions fit in 32 bits: total_q and the pool's slot count are checked
+// below 2^31 on the host, and ctx is clamped to the table's reach.
+struct Item {
+  int seq, kvh, ntiles;
+  int q0, C, ctx, prefix, p0;
 };
 
-template <typename T>
+// Item idx of the schedule: pair index descending (largest query positions,
+// hence longest key ranges, first), then sequence, then KV head.  False for
+// items with no query rows.
+__device__ __forceinline__ bool item_at(const TcParams& p, int idx, int N, Item& it) {
+  const int per_pair = p.num_seqs * p.Hkv;
+  const int pair = p.pairs - 1 - idx / per_pair;
+  const int rem = idx - (idx / per_pair) * per_pair;
+  it.seq = rem / p.Hkv;
+  it.kvh = rem - it.seq * p.Hkv;
+  const int64_t q0 = __ldg(p.cu_q + it.seq);
+  const int64_t C = __ldg(p.cu_q + it.seq + 1) - q0;
+  int64_t ctx = __ldg(p.context_lens + it.seq);
+  if (ctx > p.ctx_cap) ctx = p.ctx_cap;
+  if (C <= 0 || C > ctx || q0 < 0 || q0 + C > p.total_q) return false;
+  it.q0 = static_cast<int>(q0);
+  it.C = static_cast<int>(C);
+  it.ctx = static_cast<int>(ctx);
+  it.prefix = it.ctx - it.C;
+  it.p0 = pair * 2 * p.P;
+  if (it.p0 >= it.C) return false;
+  const int last = it.prefix + min(it.C, it.p0 + 2 * p.P) - 1;
+  it.ntiles = last / N + 1;
+  return true;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b) { return MmaOp<T>::pack(a, b); }
+
+template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                                                 const __grid_constant__ CUtensorMap tmap_k,
                                                                 const __grid_constant__ CUtensorMap tmap_v,
                                                                 TcParams p) {
+  using L = Lay<D>;
+  constexpr int N = L::N, ST = L::ST, QB = L::QB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + kStages;
-  uint64_t* s_full = kv_empty + kStages;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_full = p_full + 2;
-  uint64_t* o_free = o_full + 2;
-  uint64_t* mma_done = o_free + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffTmem);
+  uint64_t* q_empty = q_full + QB;
+  uint64_t* kv_full = q_empty + QB;
+  uint64_t* kv_empty = kv_full + ST;
+  uint64_t* s_full = kv_empty + ST;   // [2], MMA commit
+  uint64_t* p_full = s_full + 2;      // [2], 128 softmax arrivals
+  uint64_t* o_ready = p_full + 2;     // [2], MMA commit after an item's last P V
+  uint64_t* o_empty = o_ready + 2;    // [2], 128 arrivals once O is read out
+  uint64_t* mma_done = o_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int seq = blockIdx.z, kvh = blockIdx.y;
-  const int mt = p.mtiles - 1 - static_cast<int>(blockIdx.x);
-  const int64_t q0 = p.cu_q[seq];
-  const int64_t C = p.cu_q[seq + 1] - q0;
-  int64_t ctx = p.context_lens[seq];
-  const int64_t cap = p.bt_width * (int64_t)p.bs;
-  if (ctx > cap) ctx = cap;
-  const int64_t prefix = ctx - C;
-  const int64_t p0 = (int64_t)mt * p.P;
-  if (C <= 0 || prefix < 0 || p0 >= C) return;  // uniform for the CTA
-  const int np = static_cast<int>(min((int64_t)p.P, C - p0));
-  const int64_t Lmin = prefix + p0;
-  const int64_t Lmax = prefix + p0 + np - 1;
-  const int ntiles = static_cast<int>(Lmax / kN) + 1;
-  const int nfull = static_cast<int>((Lmin + 1) / kN);  // tiles below need no mask
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < QB; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < ST; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 128);
+      mbar_init(&o_ready[i], 1);
+      mbar_init(&o_empty[i], 128);
     }
     mbar_init(mma_done, 1);
+    *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kMmaWarp) {
+    tc::tmem_alloc(tmem_slot, L::kTmemCols);
     tc::tmem_relinquish();
+  }
+  if (warp == kProducerWarp) {
+    // Q rows past G*P are never written by TMA: zero them once.
+    const int live = p.G * p.P;
+    const int dead_chunks = (kM - live) * 8;  // 16-byte chunks per slab
+    for (int t = 0; t < QB * 2 * L::kDH; ++t)
+      for (int c = lane; c < dead_chunks; c += 32)
+        *reinterpret_cast<int4*>(smem + L::kOffQ + t * L::kSlab + live * 128 + c * 16) = make_int4(0, 0, 0, 0);
+    fence_proxy_async_smem();
   }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtrlRegs));
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       prefetch_tensormap(&tmap_q);
       prefetch_tensormap(&tmap_k);
       prefetch_tensormap(&tmap_v);
-      const int qrows = p.G * p.P;
-      for (int r = qrows; r < kM; ++r)
-        for (int c = 0; c < 8; ++c) *reinterpret_cast<int4*>(smem + kOffQ + r * 128 + c * 16) = make_int4(0, 0, 0, 0);
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(q_full, qrows * 128);
-      tma_load_3d(smem + kOffQ, &tmap_q, q_full, 0, kvh * p.G, static_cast<int>(q0 + p0));
-      const int64_t* bt_row = p.bt + (int64_t)seq * p.bt_stride;
-      bool ok = true;
-      int issued = 0;
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages) ok = mbar_wait(&kv_empty[st], ((j / kStages) - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-        if (!ok) break;
-        ++issued;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kTileBytes);
-        for (int i = 0; i < kN / 16; ++i) {
-          const int64_t tok = (int64_t)j * kN + i * 16;
-          int y = static_cast<int>(p.num_slots);  // out of range -> zero fill
-          if (tok < ctx) {
-            const int64_t pb = bt_row[tok / p.bs];
-            y = static_cast<int>(pb * p.bs + tok % p.bs);
-          }
-          tma_load_3d(smem + kOffK + st * kTileBytes + i * 2048, &tmap_k, &kv_full[st], 0, kvh, y);
-          tma_load_3d(smem + kOffV + st * kTileBytes + i * 2048, &tmap_v, &kv_full[st], 0, kvh, y);
+    }
+    uint32_t li = 0, g = 0;  // Q loads issued (one per item), K/V tiles issued
+    bool ok = true;
+    for (int idx = blockIdx.x; idx < p.num_items && ok; idx += gridDim.x) {
+      Item it;
+      if (!item_at(p, idx, N, it)) continue;
+      const int qb = li % QB;
+      if (lane == 0) {
+        if (*abort_flag) ok = false;
+        if (ok && li >= (uint32_t)QB)
+          ok = mbar_wait(&q_empty[qb], ((li / QB) - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+        if (ok) {
+          mbar_arrive_expect_tx(&q_full[qb], 2 * L::kDH * p.G * p.P * 128);
+          for (int w = 0; w < 2; ++w)
+            for (int dh = 0; dh < L::kDH; ++dh)
+              tma_load_3d(smem + L::kOffQ + (qb * 2 + w) * L::kQTile + dh * L::kSlab, &tmap_q, &q_full[qb],
+                          dh * 64, it.kvh * p.G, it.q0 + it.p0 + w * p.P);
         }
       }
-      // Copies still in flight (only on an aborted run) must land before exit.
-      for (int j = max(0, issued - kStages); j < issued; ++j)
-        mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      ++li;
+      const int64_t* bt_row = p.bt + (int64_t)it.seq * p.bt_stride;
+      for (int j = 0; j < it.ntiles && ok; ++j, ++g) {
+        const int st = g % ST;
+        if (lane == 0) {
+          if (*abort_flag) ok = false;
+          if (ok && g >= (uint32_t)ST)
+            ok = mbar_wait(&kv_empty[st], ((g / ST) - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+          if (ok) mbar_arrive_expect_tx(&kv_full[st], 2 * L::kKVTile);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (lane < L::kBoxes) {
+          const int grp = lane % (N / kBoxTokens), dh = lane / (N / kBoxTokens);
+          const int tok = j * N + grp * kBoxTokens;
+          int y = static_cast<int>(p.num_slots);  // out of range -> zero fill
+          if (tok < it.ctx) {
+            const int64_t pb = __ldg(bt_row + tok / p.bs);
+            if (pb >= 0 && pb < p.num_blocks) y = static_cast<int>(pb) * p.bs + tok % p.bs;
+          }
+          const int off = st * L::kKVTile + dh * N * 128 + grp * kBoxTokens * 128;
+          tma_load_3d(smem + L::kOffK + off, &tmap_k, &kv_full[st], dh * 64, it.kvh, y);
+          tma_load_3d(smem + L::kOffV + off, &tmap_v, &kv_full[st], dh * 64, it.kvh, y);
+        }
+        __syncwarp();
+      }
     }
-  } else if (warp == 1) {
+    if (!ok && lane == 0) *abort_flag = 1;
+    // Copies still in flight (only after an abort) land before exit: the
+    // last phase of every stage / Q buffer that was used.
+    if (lane == 0) {
+      for (uint32_t x = (g > (uint32_t)ST ? g - ST : 0); x < g; ++x)
+        mbar_wait(&kv_full[x % ST], (x / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+      for (uint32_t x = (li > (uint32_t)QB ? li - QB : 0); x < li; ++x)
+        mbar_wait(&q_full[x % QB], (x / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+    }
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-      constexpr uint32_t idesc_s = tc::instr_desc_f16(kBf16, kM, kN, false, false);
-      constexpr uint32_t idesc_o = tc::instr_desc_f16(kBf16, kM, kD, false, true);
-      bool ok = mbar_wait(q_full, 0, p.status, PA_DEVICE_TIMEOUT_TMA);
-      tc::fence_after_sync();
-      const uint32_t qaddr = smem_u32(smem + kOffQ);
-      for (int j = 0; j <= ntiles && ok; ++j) {
-        if (j < ntiles) {
-          const int st = j % kStages;
-          ok = mbar_wait(&kv_full[st], (j / kStages) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+      constexpr uint32_t idesc_s = tc::instr_desc_f16(kBf16, kM, N, false, false);
+      constexpr uint32_t idesc_o = tc::instr_desc_f16(kBf16, kM, D, false, true);
+      const uint32_t sbase = smem_u32(smem);
+      uint32_t li = 0, g = 0;
+      bool ok = true;
+      // O_w += P_w V(stage) for the tile whose softmax was the t-th of group w.
+      auto issue_pv = [&](int w, uint32_t t, int stage, bool accumulate, bool first_of_item) {
+        if (ok) ok = mbar_wait(&p_full[w], t & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+        if (ok && first_of_item && li > 0) ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+        if (!ok) return;
+        tc::fence_after_sync();
+        const uint32_t pa = sbase + L::kOffP + w * L::kPTile;
+        const uint32_t va = sbase + L::kOffV + stage * L::kKVTile;
+#pragma unroll
+        for (int kk = 0; kk < N / 16; ++kk) {
+          const uint64_t a = tc::smem_desc_sw128(pa + (kk >> 2) * L::kSlab + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = tc::smem_desc_sw128(va + kk * 2048, N * 128, 1024);
+          tc::mma_ss(tmem + L::kTmemO + w * D, a, b, idesc_o, accumulate || kk > 0);
+        }
+      };
+      auto issue_s = [&](int w, int qb, int stage) {
+        const uint32_t qa = sbase + L::kOffQ + (qb * 2 + w) * L::kQTile;
+        const uint32_t ka = sbase + L::kOffK + stage * L::kKVTile;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a = tc::smem_desc_sw128(qa + (kk >> 2) * L::kSlab + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = tc::smem_desc_sw128(ka + (kk >> 2) * N * 128 + (kk & 3) * 32, 16, 1024);
+          tc::mma_ss(tmem + L::kTmemS + w * N, a, b, idesc_s, kk > 0);
+        }
+        tc::commit(&s_full[w]);
+      };
+      for (int idx = blockIdx.x; idx < p.num_items && ok; idx += gridDim.x) {
+        Item it;
+        if (!item_at(p, idx, N, it)) continue;
+        const int qb = li % QB;
+        ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+        for (int j = 0; j < it.ntiles && ok; ++j, ++g) {
+          const int st = g % ST;
+          ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+          if (ok && *abort_flag) ok = false;
           if (!ok) break;
           tc::fence_after_sync();
-          const uint32_t kaddr = smem_u32(smem + kOffK + st * kTileBytes);
-          const uint32_t d_s = tmem + kTmemS + (j & 1) * kN;
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            tc::mma_ss(d_s, tc::smem_desc_sw128(qaddr + kk * 32, 16, 1024),
-                       tc::smem_desc_sw128(kaddr + kk * 32, 16, 1024), idesc_s, kk > 0);
+          for (int w = 0; w < 2 && ok; ++w) {
+            if (j > 0) issue_pv(w, g - 1, (g - 1) % ST, j > 1, j == 1);
+            if (ok) issue_s(w, qb, st);
           }
-          tc::commit(&s_full[j & 1]);
+          if (ok && j > 0) tc::commit(&kv_empty[(g - 1) % ST]);
         }
-        if (j >= 1) {
-          const int jp = j - 1, b = jp & 1, stp = jp % kStages;
-          ok = mbar_wait(&p_full[b], (jp >> 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-          if (ok && jp >= 2) ok = mbar_wait(&o_free[b], ((jp >> 1) - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-          if (!ok) break;
-          tc::fence_after_sync();
-          const uint32_t paddr = smem_u32(smem + kOffP + b * kPBytes);
-          const uint32_t vaddr = smem_u32(smem + kOffV + stp * kTileBytes);
-          const uint32_t d_o = tmem + kTmemO + b * kD;
-#pragma unroll
-          for (int kk = 0; kk < kN / 16; ++kk) {
-            const uint64_t a = tc::smem_desc_sw128(paddr + (kk >> 2) * (kM * 128) + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = tc::smem_desc_sw128(vaddr + kk * 2048, 16, 1024);
-            tc::mma_ss(d_o, a, bd, idesc_o, kk > 0);
-          }
-          tc::commit(&o_full[b]);
-          tc::commit(&kv_empty[stp]);
+        if (!ok) break;
+        // Last P V of the item, then release its Q buffer and O.
+        for (int w = 0; w < 2 && ok; ++w) {
+          issue_pv(w, g - 1, (g - 1) % ST, it.ntiles > 1, it.ntiles == 1);
+          if (ok) tc::commit(&o_ready[w]);
         }
+        if (!ok) break;
+        tc::commit(&kv_empty[(g - 1) % ST]);
+        tc::commit(&q_empty[qb]);
+        ++li;
       }
-      // Every MMA this thread issued has retired before TMEM is released
-      // (immediate on the normal path; bounded on an aborted one).
+      if (!ok) *abort_flag = 1;
+      // Every MMA issued has retired before TMEM is released.
       tc::commit(mma_done);
       mbar_wait(mma_done, 0, p.status, PA_DEVICE_TIMEOUT_MMA);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // ------------------------------------------------------------ softmax
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const int pl = r / p.G, hj = r - pl * p.G;
-    const bool row_live = (r < p.G * p.P) && (pl < np);
-    const int64_t Lr = prefix + p0 + min(pl, np - 1);
+    const int w = warp >> 2;                 // M-tile of this group
+    const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;       // row of the M-tile = TMEM lane
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-    float oacc[kD];
-#pragma unroll
-    for (int d = 0; d < kD; ++d) oacc[d] = 0.f;
+    const int pl = r / p.G, hj = r - (r / p.G) * p.G;
+    const bool row_in_tile = r < p.G * p.P;
+    uint32_t li = 0, t = 0;
     bool ok = true;
-    // Iteration j: softmax of tile j (j < ntiles), then fold O_{j-1} into
-    // the register accumulator while the tensor core computes O_j / S_{j+1}.
-    for (int j = 0; j <= ntiles; ++j) {
-      float alpha = 1.f;
-      if (j < ntiles) {
-        const int b = j & 1;
-        if (ok) ok = mbar_wait(&s_full[b], (j >> 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+    for (int idx = blockIdx.x; idx < p.num_items && ok; idx += gridDim.x) {
+      Item it;
+      if (!item_at(p, idx, N, it)) continue;
+      const int p0w = it.p0 + w * p.P;
+      const int npw = max(0, min(p.P, it.C - p0w));
+      const bool live = row_in_tile && pl < npw;
+      const int Lr = it.prefix + p0w + min(pl, max(npw - 1, 0));
+      const int nfull = (it.prefix + p0w + 1) / N;
+      float m_run = -INFINITY, l = 0.f;
+      for (int j = 0; j < it.ntiles; ++j, ++t) {
+        ok = mbar_wait(&s_full[w], t & 1, p.status, PA_DEVICE_TIMEOUT_MMA) && !*abort_flag;
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
         tc::fence_after_sync();
-        uint32_t su[kN];
+        uint32_t su[N];  // S row as raw bits
 #pragma unroll
-        for (int c = 0; c < kN / 32; ++c) tc::tmem_ld32(lane_addr + kTmemS + b * kN + c * 32, su + c * 32);
+        for (int c = 0; c < N / 32; ++c) tc::tmem_ld32(lane_addr + L::kTmemS + w * N + c * 32, su + c * 32);
         tc::tmem_wait_ld();
-        float sv[kN];
-#pragma unroll
-        for (int k = 0; k < kN; ++k) sv[k] = __uint_as_float(su[k]);
         if (j >= nfull) {
-          const int64_t lim64 = Lr - (int64_t)j * kN;  // keep tokens k <= lim
-          const int lim = static_cast<int>(lim64 > kN ? kN : lim64);
+          const int lim = Lr - j * N;  // keep keys k <= lim
 #pragma unroll
-          for (int k = 0; k < kN; ++k) sv[k] = (k <= lim) ? sv[k] : -INFINITY;
+          for (int k = 0; k < N; ++k) su[k] = (k <= lim) ? su[k] : 0xff800000u;  // -inf
         }
-        float mx = sv[0];
+#define SV(k) __uint_as_float(su[k])
+        float mx8[8];
 #pragma unroll
-        for (int k = 1; k < kN; ++k) mx = fmaxf(mx, sv[k]);
-        const float m_new = fmaxf(m, mx * p.scale_log2);
-        alpha = exp2f(m - m_new);
-        if (j == ntiles - 1) {
-          // V rows past the context (stale or NaN-poisoned slots of the last
-          // block) are zeroed so that 0-probability columns stay exactly 0.
-          const int64_t tok = (int64_t)j * kN + r;
-          if (tok >= ctx) {
-            if (ok) ok = mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-            uint8_t* vrow = smem + kOffV + (j % kStages) * kTileBytes + r * 128;
+        for (int i = 0; i < 8; ++i) mx8[i] = SV(i);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) *reinterpret_cast<int4*>(vrow + c * 16) = make_int4(0, 0, 0, 0);
+        for (int k = 8; k < N; ++k) mx8[k & 7] = fmaxf(mx8[k & 7], SV(k));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
+        if (j == 0) {
+          m_run = mx;  // key 0 is always visible: finite
+        } else {
+          const float m_new = fmaxf(m_run, mx);
+          const bool need = m_new > m_run + kRescaleLog2;
+          if (__any_sync(0xffffffffu, need)) {
+            // O_w holds P V up to tile j-1 (complete: the commit behind
+            // s_full covered it).  Scale the rows that need it in TMEM.
+            const float alpha = need ? fast_exp2(m_run - m_new) : 1.f;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t ov[32];
+              tc::tmem_ld32(lane_addr + L::kTmemO + w * D + c * 32, ov);
+              tc::tmem_wait_ld();
+#pragma unroll
+              for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
+              tc::tmem_st32(lane_addr + L::kTmemO + w * D + c * 32, ov);
+            }
+            tc::tmem_wait_st();
+            if (need) {
+              l *= alpha;
+              m_run = m_new;
+            }
           }
         }
-        float sum = 0.f;
-        uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
+        if (w == 0 && j == it.ntiles - 1 && r < N) {
+          // V rows past the context (stale or poisoned slots of the last
+          // block) are zeroed so 0-probability columns contribute exactly 0.
+          const int tok = j * N + r;
+          if (tok >= it.ctx) {
+            const int st = t % ST;
+            if (mbar_wait(&kv_full[st], (t / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA)) {
 #pragma unroll
-        for (int c = 0; c < kN / 8; ++c) {
+              for (int dh = 0; dh < L::kDH; ++dh) {
+                uint8_t* vrow = smem + L::kOffV + st * L::kKVTile + dh * N * 128 + r * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) *reinterpret_cast<int4*>(vrow + c * 16) = make_int4(0, 0, 0, 0);
+              }
+            }
+          }
+        }
+        float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        uint8_t* prow = smem + L::kOffP + w * L::kPTile + r * 128;
+#pragma unroll
+        for (int c = 0; c < N / 8; ++c) {
           float e[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            e[i] = exp2f(fmaf(sv[c * 8 + i], p.scale_log2, -m_new));
-            sum += e[i];
+            e[i] = fast_exp2(fmaf(SV(c * 8 + i), p.scale_log2, -m_run));
+            sum8[i] += e[i];
           }
           int4 v;
-          v.x = static_cast<int>(Pack2<T>::run(e[0], e[1]));
-          v.y = static_cast<int>(Pack2<T>::run(e[2], e[3]));
-          v.z = static_cast<int>(Pack2<T>::run(e[4], e[5]));
-          v.w = static_cast<int>(Pack2<T>::run(e[6], e[7]));
-          const int chunk = c & 7;
-          *reinterpret_cast<int4*>(prow + (c >> 3) * (kM * 128) + ((chunk ^ (r & 7)) << 4)) = v;
+          v.x = static_cast<int>(pack2<T>(e[0], e[1]));
+          v.y = static_cast<int>(pack2<T>(e[2], e[3]));
+          v.z = static_cast<int>(pack2<T>(e[4], e[5]));
+          v.w = static_cast<int>(pack2<T>(e[6], e[7]));
+          *reinterpret_cast<int4*>(prow + (c >> 3) * L::kSlab + (((c & 7) ^ (r & 7)) << 4)) = v;
         }
-        l = l * alpha + sum;
-        m = m_new;
+#undef SV
+        l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
         fence_proxy_async_smem();
         tc::fence_before_sync();
-        mbar_arrive(&p_full[b]);
+        mbar_arrive(&p_full[w]);
       }
-      if (j >= 1) {
-        const int jt = j - 1, bo = jt & 1;
-        if (ok) ok = mbar_wait(&o_full[bo], (jt >> 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-        tc::fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < kD / 32; ++c) {
-          uint32_t ov[32];
-          tc::tmem_ld32(lane_addr + kTmemO + bo * kD + c * 32, ov);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int d = 0; d < 32; ++d)
-            oacc[c * 32 + d] = fmaf(oacc[c * 32 + d], alpha_prev, __uint_as_float(ov[d]));
-        }
-        tc::fence_before_sync();
-        mbar_arrive(&o_free[bo]);
-      }
-      alpha_prev = alpha;
-    }
-
-    if (row_live) {
+      if (!ok) break;
+      // Epilogue: the item's last P V has landed in O_w.
+      ok = mbar_wait(&o_ready[w], li & 1, p.status, PA_DEVICE_TIMEOUT_MMA) && !*abort_flag;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc::fence_after_sync();
       const float inv = 1.f / l;
-      T* out = reinterpret_cast<T*>(p.out) + (q0 + p0 + pl) * p.o_s0 + (int64_t)(kvh * p.G + hj) * p.o_s1;
+      T* out = reinterpret_cast<T*>(p.out) + (int64_t)(it.q0 + p0w + pl) * p.o_s0 +
+               (int64_t)(it.kvh * p.G + hj) * p.o_s1;
 #pragma unroll
-      for (int c = 0; c < kD / 8; ++c) {
-        int4 v;
-        v.x = static_cast<int>(Pack2<T>::run(oacc[c * 8 + 0] * inv, oacc[c * 8 + 1] * inv));
-        v.y = static_cast<int>(Pack2<T>::run(oacc[c * 8 + 2] * inv, oacc[c * 8 + 3] * inv));
-        v.z = static_cast<int>(Pack2<T>::run(oacc[c * 8 + 4] * inv, oacc[c * 8 + 5] * inv));
-        v.w = static_cast<int>(Pack2<T>::run(oacc[c * 8 + 6] * inv, oacc[c * 8 + 7] * inv));
-        *reinterpret_cast<int4*>(out + c * 8) = v;
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ov[32];
+        tc::tmem_ld32(lane_addr + L::kTmemO + w * D + c * 32, ov);
+        tc::tmem_wait_ld();
+        if (live) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            int4 v;
+            v.x = static_cast<int>(pack2<T>(__uint_as_float(ov[q * 8 + 0]) * inv, __uint_as_float(ov[q * 8 + 1]) * inv));
+            v.y = static_cast<int>(pack2<T>(__uint_as_float(ov[q * 8 + 2]) * inv, __uint_as_float(ov[q * 8 + 3]) * inv));
+            v.z = static_cast<int>(pack2<T>(__uint_as_float(ov[q * 8 + 4]) * inv, __uint_as_float(ov[q * 8 + 5]) * inv));
+            v.w = static_cast<int>(pack2<T>(__uint_as_float(ov[q * 8 + 6]) * inv, __uint_as_float(ov[q * 8 + 7]) * inv));
+            *reinterpret_cast<int4*>(out + c * 32 + q * 8) = v;
+          }
+        }
       }
+      tc::fence_before_sync();
+      mbar_arrive(&o_empty[w]);
+      ++li;
     }
+    if (!ok) *abort_flag = 1;
   }
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, kTmemCols);
+    tc::tmem_dealloc(tmem, L::kTmemCols);
   }
 }
 
@@ -343,12 +489,41 @@ int current_device_id() {
   return d;
 }
 
+template <typename T, int D>
+int launch_typed(const PrefillTcArgs& a, const TcParams& p, cudaStream_t st) {
+  using L = Lay<D>;
+  CUtensorMap tq, tk, tv;
+  const int es = 2;
+  if (make_map_3d(&tq, a.dtype, a.q, D, a.Hq, a.total_q, (uint64_t)a.q_s1 * es, (uint64_t)a.q_s0 * es, 64, a.group,
+                  p.P, CU_TENSOR_MAP_SWIZZLE_128B) != PA_OK)
+    return PA_ERR_CUDA;
+  const uint64_t s1b = (uint64_t)D * es, s2b = s1b * a.Hkv;
+  if (make_map_3d(&tk, a.dtype, a.kp, D, a.Hkv, p.num_slots, s1b, s2b, 64, 1, kBoxTokens,
+                  CU_TENSOR_MAP_SWIZZLE_128B) != PA_OK ||
+      make_map_3d(&tv, a.dtype, a.vp, D, a.Hkv, p.num_slots, s1b, s2b, 64, 1, kBoxTokens,
+                  CU_TENSOR_MAP_SWIZZLE_128B) != PA_OK)
+    return PA_ERR_CUDA;
+  static bool attr_done[64] = {};
+  const int dev = current_device_id();
+  if (dev < 0 || dev >= 64) return PA_ERR_CUDA;
+  auto kern = prefill_tc_kernel<T, D>;
+  if (!attr_done[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kSmem) != cudaSuccess)
+      return PA_ERR_CUDA;
+    attr_done[dev] = true;
+  }
+  const int grid = std::min(p.num_items, num_sms(dev));
+  kern<<<grid, kThreads, L::kSmem, st>>>(tq, tk, tv, p);
+  PA_CHECK_LAUNCH();
+  return PA_OK;
+}
+
 }  // namespace
 
 bool prefill_tc_supported(const PrefillTcArgs& a) {
   if (a.dtype != PA_DTYPE_BF16 && a.dtype != PA_DTYPE_F16) return false;
-  if (a.D != kD) return false;
-  if (a.bs % 16 != 0 || a.bs > 256) return false;
+  if (a.D != 64 && a.D != 128) return false;
+  if (a.bs % kBoxTokens != 0) return false;
   if (a.group < 1 || a.group > kM) return false;
   if (a.num_blocks * (int64_t)a.bs >= (int64_t(1) << 31) || a.total_q >= (int64_t(1) << 31)) return false;
   if (a.max_q_len <= 0) return false;
@@ -365,44 +540,28 @@ int launch_prefill_tc(const PrefillTcArgs& a, cudaStream_t st) {
   p.bt = a.bt;
   p.bt_stride = a.bt_stride;
   p.bt_width = a.bt_width;
+  p.num_blocks = a.num_blocks;
   p.num_slots = a.num_blocks * (int64_t)a.bs;
+  p.ctx_cap = std::min<int64_t>(a.bt_width * (int64_t)a.bs, (int64_t(1) << 31) - 1);
+  p.total_q = a.total_q;
   p.out = a.out;
   p.o_s0 = a.o_s0;
   p.o_s1 = a.o_s1;
   p.G = a.group;
   p.P = kM / a.group;
   p.bs = a.bs;
-  p.mtiles = (a.max_q_len + p.P - 1) / p.P;
+  p.Hkv = a.Hkv;
+  p.num_seqs = a.num_seqs;
+  p.pairs = (a.max_q_len + 2 * p.P - 1) / (2 * p.P);
+  const int64_t items = (int64_t)p.pairs * a.num_seqs * a.Hkv;
+  if (items <= 0) return PA_OK;
+  if (items >= (int64_t(1) << 31)) return PA_ERR_INVALID;
+  p.num_items = static_cast<int>(items);
   p.scale_log2 = a.scale * 1.4426950408889634f;
   p.status = a.status;
-
-  CUtensorMap tq, tk, tv;
-  const int es = 2;
-  if (make_map_3d(&tq, a.dtype, a.q, kD, a.Hq, a.total_q, (uint64_t)a.q_s1 * es, (uint64_t)a.q_s0 * es, kD,
-                  a.group, p.P, CU_TENSOR_MAP_SWIZZLE_128B) != PA_OK)
-    return PA_ERR_CUDA;
-  const uint64_t s1b = (uint64_t)kD * es, s2b = s1b * a.Hkv;
-  if (make_map_3d(&tk, a.dtype, a.kp, kD, a.Hkv, p.num_slots, s1b, s2b, kD, 1, 16, CU_TENSOR_MAP_SWIZZLE_128B) !=
-          PA_OK ||
-      make_map_3d(&tv, a.dtype, a.vp, kD, a.Hkv, p.num_slots, s1b, s2b, kD, 1, 16, CU_TENSOR_MAP_SWIZZLE_128B) !=
-          PA_OK)
-    return PA_ERR_CUDA;
-
-  static bool attr_done[2][64] = {};
-  const int dev = current_device_id();
-  if (dev < 0 || dev >= 64) return PA_ERR_CUDA;
-  const int ti = a.dtype == PA_DTYPE_BF16 ? 0 : 1;
-  auto kern = a.dtype == PA_DTYPE_BF16 ? prefill_tc_kernel<__nv_bfloat16> : prefill_tc_kernel<__half>;
-  if (!attr_done[ti][dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) != cudaSuccess)
-      return PA_ERR_CUDA;
-    attr_done[ti][dev] = true;
-  }
-  if (a.num_seqs > 65535 || a.Hkv > 65535) return PA_ERR_INVALID;
-  dim3 grid(p.mtiles, a.Hkv, a.num_seqs);
-  kern<<<grid, kThreads, kSmem, st>>>(tq, tk, tv, p);
-  PA_CHECK_LAUNCH();
-  return PA_OK;
+  const bool bf16 = a.dtype == PA_DTYPE_BF16;
+  if (a.D == 64) return bf16 ? launch_typed<__nv_bfloat16, 64>(a, p, st) : launch_typed<__half, 64>(a, p, st);
+  return bf16 ? launch_typed<__nv_bfloat16, 128>(a, p, st) : launch_typed<__half, 128>(a, p, st);
 }
 
 }  // namespace pa

@@ -120,3 +120,33 @@ def test_config4_geometry(cuda_device, dtype):
         q = case["q_np"][case["cu_np"][s] : case["cu_np"][s + 1]]
         exp.append(O.prefill_chunk(q, k_np, v_np, case["np"][3][s], prefix[s], prefix[s] + 512, 16))
     check(out, np.concatenate(exp, 0), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv,d", [(14, 2, 64), (28, 4, 128), (8, 8, 64), (16, 1, 128)])
+def test_many_items_per_cta(cuda_device, dtype, hq, hkv, d):
+    """More work items than SMs, so each persistent CTA runs several items
+    back to back (Q buffers and O accumulators recycled across items), with
+    ragged chunks, empty-prefix and long-prefix sequences mixed."""
+    rng = np.random.default_rng(hq * d + hkv)
+    nseq = 40
+    prefix = rng.integers(0, 700, size=nseq).tolist()
+    chunk = rng.integers(1, 300, size=nseq).tolist()
+    prefix[0], chunk[0] = 0, 299
+    prefix[1], chunk[1] = 2900, 260
+    case = make_prefill_case(prefix, chunk, hq, hkv, d, 16, dtype, cuda_device, seed=hq + 3 * d)
+    out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
+                                         case["max_q"])
+    check(out, oracle_prefill(case), dtype)
+    # Same call again: the kernel keeps no state between launches.
+    out2 = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
+                                          case["max_q"])
+    assert torch.equal(out, out2)
+
+
+def test_prefill_block_size_32(cuda_device):
+    """Blocks of 32 tokens: two 16-token TMA boxes per table entry."""
+    case = make_prefill_case([0, 100, 31], [64, 90, 1], 14, 2, 64, 32, torch.bfloat16, cuda_device, seed=3)
+    out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
+                                         case["max_q"])
+    check(out, oracle_prefill(case), torch.bfloat16)

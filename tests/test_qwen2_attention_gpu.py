@@ -57,8 +57,10 @@ def test_batch_decode_matches_single_requests(cuda_device, num_kv_heads, batch_s
         actual = attention.forward_decode_batch_with_cache(kv_cache=cache, **inputs)
     assert actual.shape == inputs["hidden_states"].shape
     torch.testing.assert_close(actual, expected, rtol=1e-5, atol=1e-6)
-    assert torch.equal(cache.k_cache, ref_cache.k_cache)
-    assert torch.equal(cache.v_cache, ref_cache.v_cache)
+    # Batched and one-row projections may round differently (cuBLAS picks
+    # another kernel per M): close, as in the reference's own test.
+    torch.testing.assert_close(cache.k_cache, ref_cache.k_cache)
+    torch.testing.assert_close(cache.v_cache, ref_cache.v_cache)
     unchanged = torch.ones(cache.k_cache.shape[:3], dtype=torch.bool, device=cuda_device)
     s = inputs["slot_mapping"]
     unchanged[1, s // 2, s % 2] = False
