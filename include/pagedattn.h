@@ -54,6 +54,9 @@ extern "C" {
 #define PA_DTYPE_BF16 2
 #define PA_DTYPE_F64 3
 
+/* Ints in the control block of pa_chunk_prefill. */
+#define PA_PREFILL_CONTROL_INTS 4
+
 /* Human-readable name of a status code (static storage). */
 PA_API const char* pa_status_string(int status);
 
@@ -171,16 +174,22 @@ PA_API int pa_paged_decode_noalloc(const void* q, int64_t q_s0, int64_t q_s1, co
  * context_lens : [num_seqs] int64
  * block_tables : [num_seqs, bt_width] int64, row stride bt_stride
  * out          : [total_q, Hq, D], element strides (o_s0, o_s1)
- * max_q_len    : upper bound of any chunk length (sizes the launch grid)
- * status       : optional device int (may be NULL); the tensor-core kernel
- *                records PA_DEVICE_TIMEOUT_* there if a bounded wait gives up
+ * max_q_len    : upper bound of any chunk length (sizes the work list)
+ * control      : optional device int[PA_PREFILL_CONTROL_INTS], all zero
+ *                before the first call (may be NULL).  control[0] receives
+ *                PA_DEVICE_TIMEOUT_* if a bounded wait of the tensor-core
+ *                kernel gives up; control[1..2] are the work-claim counters
+ *                of its dynamic schedule, which every call leaves at zero
+ *                again.  Calls that share a control block must not overlap
+ *                on the GPU (same stream, or ordered by events).  With NULL
+ *                the kernel falls back to a static schedule.
  */
 PA_API int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
                      const int64_t* context_lens, const int64_t* block_tables, int64_t bt_stride,
                      int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer, int64_t num_blocks,
                      int block_size, int num_kv_heads, int head_dim, void* out, int64_t o_s0, int64_t o_s1,
                      int num_seqs, int64_t total_q, int max_q_len, int num_q_heads, float scale, int dtype,
-                     int* status, void* stream);
+                     int* control, void* stream);
 
 /*
  * FP32 P.V accumulator: out[b, d] = sum_n p[b, n] * v[b, n, d] for N = 64,

@@ -143,12 +143,18 @@ def _align256(x: int) -> int:
     return (x + 255) & ~255
 
 
+PREFILL_CONTROL_INTS = 4  # PA_PREFILL_CONTROL_INTS
+
+
 def status_word(device: torch.device) -> torch.Tensor:
-    """Per-device int32 the kernels set when a bounded wait gives up."""
+    """Per-device control block of pa_chunk_prefill (int32[4], zeroed once):
+    [0] is the status the kernels set when a bounded wait gives up, [1..2]
+    the self-rewinding work-claim counters.  Calls that use it are ordered on
+    the current stream."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _status_words.get(idx)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=device)
+        t = torch.zeros(PREFILL_CONTROL_INTS, dtype=torch.int32, device=device)
         _status_words[idx] = t
     return t
 

@@ -16,7 +16,7 @@ extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const
                                 int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer,
                                 int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, void* out,
                                 int64_t o_s0, int64_t o_s1, int num_seqs, int64_t total_q, int max_q_len,
-                                int num_q_heads, float scale, int dtype, int* status, void* stream) {
+                                int num_q_heads, float scale, int dtype, int* control, void* stream) {
   using namespace pa;
   if (num_seqs < 0 || total_q < 0 || max_q_len < 0 || num_kv_heads <= 0 || num_q_heads <= 0 ||
       num_q_heads % num_kv_heads != 0 || head_dim <= 0 || block_size <= 0 || num_blocks <= 0 || bt_width <= 0)
@@ -54,7 +54,7 @@ extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const
   a.max_q_len = max_q_len;
   a.scale = scale;
   a.dtype = dtype;
-  a.status = status;
+  a.control = control;
   if (prefill_tc_supported(a)) return launch_prefill_tc(a, st);
 
   GenericParams g;

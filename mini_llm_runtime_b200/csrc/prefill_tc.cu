@@ -10,9 +10,12 @@
 // group into the 128 MMA rows: row r = (query position r / G, query head
 // r % G), P = floor(128 / G) positions per tile (18 for a group of 7 -> 126
 // live rows), so every K/V tile staged from the paged pool feeds all G query
-// heads of both M-tiles.  The kernel is persistent (one CTA per SM); CTA b
-// takes items b, b + grid, ... of a list ordered by descending query
-// position, so the longest items start first.  All roles walk the same list.
+// heads of both M-tiles.  The kernel is persistent (one CTA per SM).  Items
+// are listed by descending query position (longest key ranges first) and
+// handed out dynamically: the producer warp claims the next index from a
+// global counter (self-rewinding: the last CTA to finish zeroes it) and
+// publishes it through a small ring in shared memory to the other roles.
+// Without a control block the CTAs take every gridDim.x-th item instead.
 //
 // Warp roles (384 threads; setmaxnreg moves registers to the softmax):
 //   warp 8      TMA producer: the item's two Q tiles (3-D boxes {64, G, P}
@@ -50,12 +53,16 @@ namespace {
 constexpr int kM = 128;                      // MMA rows per M-tile
 constexpr int kThreads = 384;                // 3 warpgroups
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kConsumerWarps = 9;            // MMA warp + 8 softmax warps read each item index
 // setmaxnreg budgets (per thread): launch gives 168 x 384; the control
 // warpgroup drops to 64 so the two softmax warpgroups can hold a 128-float
 // S row: 4*32*64 + 8*32*216 <= 384*168.
 constexpr int kCtrlRegs = 64, kSoftmaxRegs = 216;
 constexpr float kRescaleLog2 = 8.f;          // lazy-rescale threshold (log2 units)
 constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
+#ifndef PA_PREFILL_POLY_PAIRS
+#define PA_PREFILL_POLY_PAIRS 0                  // of every 8 column pairs, exp2 on the FMA pipe
+#endif
 
 template <int D> struct Shape;
 // N = KV tokens per tile, ST = K/V ring stages, QB = Q buffers (items in flight).
@@ -75,9 +82,10 @@ struct Lay {
   static constexpr int kOffV = kOffK + ST * kKVTile;
   static constexpr int kOffP = kOffV + ST * kKVTile;
   static constexpr int kOffBar = kOffP + 2 * kPTile;
-  static constexpr int kNumBars = 2 * QB + 2 * ST + 8 + 1;
-  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr size_t kSmem = 1024 + kOffMisc + 16;
+  static constexpr int kRing = 4;             // claimed item indices in flight
+  static constexpr int kNumBars = 2 * QB + 2 * ST + 8 + 1 + 2 * kRing;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag, item ring
+  static constexpr size_t kSmem = 1024 + kOffMisc + 16 + 4 * kRing;
   static constexpr uint32_t kTmemS = 0;        // S_w at columns [w N, (w+1) N)
   static constexpr uint32_t kTmemO = 2 * N;    // O_w at columns [2N + w D, 2N + (w+1) D)
   static constexpr uint32_t kTmemCols = 512;
@@ -98,7 +106,9 @@ struct TcParams {
   int64_t total_q;
   int G, P, bs, Hkv, num_seqs, pairs, num_items;
   float scale_log2;
-  int* status;
+  int* status;   // control[0]; null: no status, static schedule
+  int* claim;    // control[1]: next item to hand out (dynamic schedule)
+  int* finish;   // control[2]: CTAs done; the last one zeroes claim and finish
 };
 
 // Positions fit in 32 bits: total_q and the pool's slot count are checked
@@ -133,10 +143,41 @@ __device__ __forceinline__ bool item_at(const TcParams& p, int idx, int N, Item&
   return true;
 }
 
+// 2^x on the MUFU (XU) pipe.
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
+
+// 2^x for two values on the FMA pipe (the MUFU pipe runs exp2 at a
+// sixteenth of the FMA rate, so moving part of the softmax's exponentials
+// here balances the two).  Method: Cody-Waite range reduction
+// x = n + f, n = round(x) (adding 1.5 * 2^23 rounds to an integer in the
+// low mantissa bits), |f| <= 1/2, then 2^f by a degree-3 polynomial whose
+// coefficients were fitted for minimum relative error on [-1/2, 1/2]
+// (max relative error 1.0e-4, far below the 2^-9 of the BF16/F16 P it
+// feeds), and 2^n applied by adding n to the exponent field.  Inputs are
+// clamped to >= -127 (-inf -> exactly 0); they never exceed +8 here.
+constexpr int kPolyPairsPer8 = PA_PREFILL_POLY_PAIRS;
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kShift = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -127.f);
+  x.y = fmaxf(x.y, -127.f);
+  const float2 t = __fadd2_rn(x, make_float2(kShift, kShift));
+  const float2 n = __fadd2_rn(t, make_float2(-kShift, -kShift));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(make_float2(0.0550089068f, 0.0550089068f), f, make_float2(0.242210984f, 0.242210984f));
+  q = __ffma2_rn(q, f, make_float2(0.693282962f, 0.693282962f));
+  q = __ffma2_rn(q, f, make_float2(1.f, 1.f));
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b) { return MmaOp<T>::pack(a, b); }
@@ -160,8 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* o_ready = p_full + 2;     // [2], MMA commit after an item's last P V
   uint64_t* o_empty = o_ready + 2;    // [2], 128 arrivals once O is read out
   uint64_t* mma_done = o_empty + 2;
+  uint64_t* item_full = mma_done + 1;          // [kRing], producer publishes an index
+  uint64_t* item_empty = item_full + L::kRing;  // [kRing], 9 consumer warps took it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  volatile int* ring = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -181,6 +225,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       mbar_init(&o_empty[i], 128);
     }
     mbar_init(mma_done, 1);
+    for (int i = 0; i < L::kRing; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], kConsumerWarps);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -212,10 +260,43 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       prefetch_tensormap(&tmap_v);
     }
     uint32_t li = 0, g = 0;  // Q loads issued (one per item), K/V tiles issued
+    uint32_t pub = 0;        // item indices published to the ring
+    int next_static = blockIdx.x;
     bool ok = true;
-    for (int idx = blockIdx.x; idx < p.num_items && ok; idx += gridDim.x) {
+    for (;;) {
+      // Claim the next item with query rows (dynamic: global counter;
+      // static: every gridDim.x-th) and publish its index to the consumers.
+      int idx = -1;
+      if (lane == 0) {
+        for (;;) {
+          int c;
+          if (p.claim != nullptr) {
+            c = atomicAdd(p.claim, 1);
+          } else {
+            c = next_static;
+            next_static += gridDim.x;
+          }
+          if (c >= p.num_items) break;
+          Item probe;
+          if (item_at(p, c, N, probe)) {
+            idx = c;
+            break;
+          }
+        }
+        const int rs = pub % L::kRing;
+        if (pub >= (uint32_t)L::kRing)
+          ok = mbar_wait(&item_empty[rs], ((pub / L::kRing) - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+        if (ok) {
+          ring[rs] = idx;
+          mbar_arrive(&item_full[rs]);
+          ++pub;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      idx = __shfl_sync(0xffffffffu, idx, 0);
+      if (!ok || idx < 0) break;
       Item it;
-      if (!item_at(p, idx, N, it)) continue;
+      item_at(p, idx, N, it);
       const int qb = li % QB;
       if (lane == 0) {
         if (*abort_flag) ok = false;
@@ -257,6 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
         __syncwarp();
       }
+      if (!ok) break;
     }
     if (!ok && lane == 0) *abort_flag = 1;
     // Copies still in flight (only after an abort) land before exit: the
@@ -274,6 +356,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       constexpr uint32_t idesc_s = tc::instr_desc_f16(kBf16, kM, N, false, false);
       constexpr uint32_t idesc_o = tc::instr_desc_f16(kBf16, kM, D, false, true);
       const uint32_t sbase = smem_u32(smem);
+      // Descriptor words of the first buffer of each operand (SW128, SBO
+      // 1024; V is MN-major with its 64-column halves N*128 bytes apart).
+      constexpr uint32_t kHi = tc::desc_hi_sw128(1024);
+      const uint32_t q_lo = tc::desc_lo(sbase + L::kOffQ, 16);
+      const uint32_t k_lo = tc::desc_lo(sbase + L::kOffK, 16);
+      const uint32_t v_lo = tc::desc_lo(sbase + L::kOffV, N * 128);
+      const uint32_t p_lo = tc::desc_lo(sbase + L::kOffP, 16);
       uint32_t li = 0, g = 0;
       bool ok = true;
       // O_w += P_w V(stage) for the tile whose softmax was the t-th of group w.
@@ -282,29 +371,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         if (ok && first_of_item && li > 0) ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
         if (!ok) return;
         tc::fence_after_sync();
-        const uint32_t pa = sbase + L::kOffP + w * L::kPTile;
-        const uint32_t va = sbase + L::kOffV + stage * L::kKVTile;
+        // One add per operand per MMA: offsets are compile-time (>> 4).
+        const uint32_t a0 = p_lo + w * (L::kPTile >> 4);
+        const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
+        const uint32_t d = tmem + L::kTmemO + w * D;
+        tc::mma_ss_words(d, a0, b0, kHi, idesc_o, accumulate ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < N / 16; ++kk) {
-          const uint64_t a = tc::smem_desc_sw128(pa + (kk >> 2) * L::kSlab + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = tc::smem_desc_sw128(va + kk * 2048, N * 128, 1024);
-          tc::mma_ss(tmem + L::kTmemO + w * D, a, b, idesc_o, accumulate || kk > 0);
-        }
+        for (int kk = 1; kk < N / 16; ++kk)
+          tc::mma_ss_words(d, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4), b0 + ((kk * 2048) >> 4), kHi,
+                           idesc_o, 1u);
       };
       auto issue_s = [&](int w, int qb, int stage) {
-        const uint32_t qa = sbase + L::kOffQ + (qb * 2 + w) * L::kQTile;
-        const uint32_t ka = sbase + L::kOffK + stage * L::kKVTile;
+        const uint32_t a0 = q_lo + (qb * 2 + w) * (L::kQTile >> 4);
+        const uint32_t b0 = k_lo + stage * (L::kKVTile >> 4);
+        const uint32_t d = tmem + L::kTmemS + w * N;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a = tc::smem_desc_sw128(qa + (kk >> 2) * L::kSlab + (kk & 3) * 32, 16, 1024);
-          const uint64_t b = tc::smem_desc_sw128(ka + (kk >> 2) * N * 128 + (kk & 3) * 32, 16, 1024);
-          tc::mma_ss(tmem + L::kTmemS + w * N, a, b, idesc_s, kk > 0);
-        }
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_ss_words(d, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4),
+                           b0 + (((kk >> 2) * N * 128 + (kk & 3) * 32) >> 4), kHi, idesc_s, kk > 0 ? 1u : 0u);
         tc::commit(&s_full[w]);
       };
-      for (int idx = blockIdx.x; idx < p.num_items && ok; idx += gridDim.x) {
+      for (uint32_t cons = 0; ok; ++cons) {
+        const int rs = cons % L::kRing;
+        ok = mbar_wait(&item_full[rs], (cons / L::kRing) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+        const int idx = ring[rs];
+        mbar_arrive(&item_empty[rs]);
+        if (!ok || idx < 0) break;
         Item it;
-        if (!item_at(p, idx, N, it)) continue;
+        item_at(p, idx, N, it);
         const int qb = li % QB;
         ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
         for (int j = 0; j < it.ntiles && ok; ++j, ++g) {
@@ -347,9 +441,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const bool row_in_tile = r < p.G * p.P;
     uint32_t li = 0, t = 0;
     bool ok = true;
-    for (int idx = blockIdx.x; idx < p.num_items && ok; idx += gridDim.x) {
+    for (uint32_t cons = 0; ok; ++cons) {
+      const int rs = cons % L::kRing;
+      ok = mbar_wait(&item_full[rs], (cons / L::kRing) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+      ok = __all_sync(0xffffffffu, ok);
+      const int idx = ring[rs];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[rs]);
+      if (!ok || idx < 0) break;
       Item it;
-      if (!item_at(p, idx, N, it)) continue;
+      item_at(p, idx, N, it);
       const int p0w = it.p0 + w * p.P;
       const int npw = max(0, min(p.P, it.C - p0w));
       const bool live = row_in_tile && pl < npw;
@@ -371,13 +472,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           for (int k = 0; k < N; ++k) su[k] = (k <= lim) ? su[k] : 0xff800000u;  // -inf
         }
 #define SV(k) __uint_as_float(su[k])
-        float mx8[8];
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = SV(i);
-#pragma unroll
-        for (int k = 8; k < N; ++k) mx8[k & 7] = fmaxf(mx8[k & 7], SV(k));
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
+        for (int q = 0; q < N / 2; ++q) mx4[q & 3] = fmax3(mx4[q & 3], SV(2 * q), SV(2 * q + 1));
+        const float mx = fmax3(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3], mx4[3]) * p.scale_log2;
         if (j == 0) {
           m_run = mx;  // key 0 is always visible: finite
         } else {
@@ -419,25 +517,38 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             }
           }
         }
-        float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // P = 2^(s * scale_log2 - m_run), two columns per packed FP32 op;
+        // kPolyPairsPer8 of every 8 column pairs use the FMA-pipe exp2, the
+        // rest the MUFU one, so the two pipes share the load.
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+        const float2 negm2 = make_float2(-m_run, -m_run);
+        float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         uint8_t* prow = smem + L::kOffP + w * L::kPTile + r * 128;
 #pragma unroll
         for (int c = 0; c < N / 8; ++c) {
-          float e[8];
+          uint32_t packed[4];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            e[i] = fast_exp2(fmaf(SV(c * 8 + i), p.scale_log2, -m_run));
-            sum8[i] += e[i];
+          for (int h = 0; h < 4; ++h) {
+            const int q = c * 4 + h;
+            const float2 x = __ffma2_rn(make_float2(SV(2 * q), SV(2 * q + 1)), sc2, negm2);
+            float2 e;
+            if ((q & 7) < kPolyPairsPer8) {
+              e = exp2_poly2(x);
+            } else {
+              e.x = fast_exp2(x.x);
+              e.y = fast_exp2(x.y);
+            }
+            sum2[h] = __fadd2_rn(sum2[h], e);
+            packed[h] = pack2<T>(e.x, e.y);
           }
-          int4 v;
-          v.x = static_cast<int>(pack2<T>(e[0], e[1]));
-          v.y = static_cast<int>(pack2<T>(e[2], e[3]));
-          v.z = static_cast<int>(pack2<T>(e[4], e[5]));
-          v.w = static_cast<int>(pack2<T>(e[6], e[7]));
+          const int4 v = make_int4(static_cast<int>(packed[0]), static_cast<int>(packed[1]),
+                                   static_cast<int>(packed[2]), static_cast<int>(packed[3]));
           *reinterpret_cast<int4*>(prow + (c >> 3) * L::kSlab + (((c & 7) ^ (r & 7)) << 4)) = v;
         }
 #undef SV
-        l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+        const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
+        const float2 s0123 = __fadd2_rn(s01, s23);
+        l += s0123.x + s0123.y;
         fence_proxy_async_smem();
         tc::fence_before_sync();
         mbar_arrive(&p_full[w]);
@@ -480,6 +591,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   if (warp == kMmaWarp) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, L::kTmemCols);
+  }
+  if (threadIdx.x == 0 && p.claim != nullptr) {
+    // Every claim of this CTA precedes this point; the last CTA through
+    // rewinds the counters for the next launch.
+    __threadfence();
+    if (atomicAdd(p.finish, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(p.claim, 0);
+      atomicExch(p.finish, 0);
+    }
   }
 }
 
@@ -558,7 +678,9 @@ int launch_prefill_tc(const PrefillTcArgs& a, cudaStream_t st) {
   if (items >= (int64_t(1) << 31)) return PA_ERR_INVALID;
   p.num_items = static_cast<int>(items);
   p.scale_log2 = a.scale * 1.4426950408889634f;
-  p.status = a.status;
+  p.status = a.control;
+  p.claim = a.control != nullptr ? a.control + 1 : nullptr;
+  p.finish = a.control != nullptr ? a.control + 2 : nullptr;
   const bool bf16 = a.dtype == PA_DTYPE_BF16;
   if (a.D == 64) return bf16 ? launch_typed<__nv_bfloat16, 64>(a, p, st) : launch_typed<__half, 64>(a, p, st);
   return bf16 ? launch_typed<__nv_bfloat16, 128>(a, p, st) : launch_typed<__half, 128>(a, p, st);

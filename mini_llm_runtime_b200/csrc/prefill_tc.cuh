@@ -22,7 +22,7 @@ struct PrefillTcArgs {
   int max_q_len;
   float scale;
   int dtype;
-  int* status;  // device int, may be null; first failed bounded wait is recorded
+  int* control;  // PA_PREFILL_CONTROL_INTS device ints (status, claim, finish), may be null
 };
 
 bool prefill_tc_supported(const PrefillTcArgs& a);

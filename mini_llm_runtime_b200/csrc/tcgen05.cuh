@@ -35,6 +35,29 @@ __host__ __device__ constexpr uint32_t instr_desc_f16(bool bf16, int m, int n, b
          ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// Low / high 32-bit words of a SW128 descriptor.  The start address lives
+// in bits [0,14) of the low word as addr >> 4 (< 2^14 for any shared-memory
+// address), so adding (byte offset >> 4) to the low word moves the operand
+// without touching the other fields: one integer add per MMA.
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo) {
+  return ((saddr >> 4) & 0x3FFF) | (((lbo >> 4) & 0x3FFF) << 16);
+}
+__host__ __device__ constexpr uint32_t desc_hi_sw128(uint32_t sbo) {
+  return ((sbo >> 4) & 0x3FFF) | (1u << 14) | (uint32_t(kLayoutSW128) << 29);
+}
+
+// D[tmem] (+)= A[smem] * B[smem] from split descriptor words.
+__device__ __forceinline__ void mma_ss_words(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %3};\n\t"
+      "mov.b64 db, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(accumulate));
+}
+
 // D[tmem] (+)= A[smem] * B[smem]; issued by one thread.
 __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                        bool accumulate) {

@@ -150,3 +150,29 @@ def test_prefill_block_size_32(cuda_device):
     out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
                                          case["max_q"])
     check(out, oracle_prefill(case), torch.bfloat16)
+
+
+def test_static_schedule_without_control_block(cuda_device):
+    """control = NULL: the kernel hands out items statically; same result as
+    the dynamic schedule."""
+    import ctypes
+
+    from mini_llm_runtime_b200 import _lib
+
+    case = make_prefill_case([0, 300, 1000] * 20, [200, 77, 5] * 20, 14, 2, 64, 16, torch.bfloat16, cuda_device,
+                             seed=12)
+    ref = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
+                                         case["max_q"])
+    q, out = case["q"], torch.empty_like(case["q"])
+    bt = case["tables"]
+    nb, bs, hkv, d = case["k"].shape
+    st = _lib.load().pa_chunk_prefill(
+        q.data_ptr(), q.stride(0), q.stride(1), case["cu"].data_ptr(), case["lens"].data_ptr(), bt.data_ptr(),
+        bt.stride(0), bt.shape[1], case["k"].data_ptr(), case["v"].data_ptr(), nb, bs, hkv, d, out.data_ptr(),
+        out.stride(0), out.stride(1), len(case["chunk"]), q.shape[0], case["max_q"], q.shape[1], d ** -0.5,
+        _lib.dtype_code(q.dtype), None, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == _lib.PA_OK
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    # The shared control block was left rewound by the dynamic launches.
+    assert _lib.status_word(cuda_device).tolist() == [0, 0, 0, 0]
