@@ -25,11 +25,16 @@
 //               through the block table into a ring of stages (128-byte
 //               swizzle = canonical UMMA layout).  Tokens at or past the
 //               context use an out-of-range coordinate: TMA fills zeros.
-//   warp 9      TMEM owner + single-thread MMA issuer.  Per KV tile j and
-//               M-tile w:  O_w += P_w(j-1) V(j-1)  then  S_w(j) = Q_w K(j)^T.
-//               A commit after S_w(j) therefore also covers the preceding
-//               P V, which is what lets the softmax warps rescale O_w in
-//               TMEM as soon as S_w(j) is ready.
+//   warp 9      TMEM owner + single-thread MMA issuer.  Per KV tile j:
+//               S_w(j) = Q_w K(j)^T for both M-tiles, then
+//               O_w += P_w(j-1) V(j-1) for both.
+//               S = Q K^T reads both operands from shared memory; P V reads
+//               P from tensor memory and V from shared memory, which halves
+//               the shared-memory traffic of the tile.  S, P and O of each
+//               M-tile have their own TMEM columns, so S_w(j+1) is issued as
+//               soon as the softmax has copied S_w(j) into registers: the
+//               next tile's scores are ready when the softmax finishes this
+//               one, and the P V runs behind it.
 //   warps 0-3   softmax of M-tile 0, warps 4-7 softmax of M-tile 1 (one row
 //               per thread, FP32 statistics in the log2 domain).  While one
 //               group exponentiates, the tensor core works for the other.
@@ -66,8 +71,8 @@ constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
 
 template <int D> struct Shape;
 // N = KV tokens per tile, ST = K/V ring stages, QB = Q buffers (items in flight).
-template <> struct Shape<64> { static constexpr int N = 128, ST = 3, QB = 2; };
-template <> struct Shape<128> { static constexpr int N = 64, ST = 3, QB = 1; };
+template <> struct Shape<64> { static constexpr int N = 128, ST = 4, QB = 2; };
+template <> struct Shape<128> { static constexpr int N = 64, ST = 3, QB = 2; };
 
 template <int D>
 struct Lay {
@@ -76,22 +81,28 @@ struct Lay {
   static constexpr int kSlab = kM * 128;       // one 128-row slab (16 KB)
   static constexpr int kQTile = kDH * kSlab;   // Q tile: [kDH][128 rows][128 B]
   static constexpr int kKVTile = kDH * N * 128;  // K or V tile: [kDH][N rows][128 B]
-  static constexpr int kPTile = (N / 64) * kSlab;  // P tile: [N/64][128 rows][128 B]
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + QB * 2 * kQTile;
   static constexpr int kOffV = kOffK + ST * kKVTile;
-  static constexpr int kOffP = kOffV + ST * kKVTile;
-  static constexpr int kOffBar = kOffP + 2 * kPTile;
+  static constexpr int kOffBar = kOffV + ST * kKVTile;
   static constexpr int kRing = 4;             // claimed item indices in flight
-  static constexpr int kNumBars = 2 * QB + 2 * ST + 8 + 1 + 2 * kRing;
+  static constexpr int kNumBars = 2 * QB + 2 * ST + 10 + 1 + 2 * kRing;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag, item ring
   static constexpr size_t kSmem = 1024 + kOffMisc + 16 + 4 * kRing;
-  static constexpr uint32_t kTmemS = 0;        // S_w at columns [w N, (w+1) N)
-  static constexpr uint32_t kTmemO = 2 * N;    // O_w at columns [2N + w D, 2N + (w+1) D)
+  // TMEM: 256 columns per M-tile w: S (N FP32 columns), P (N/2 columns of
+  // packed 16-bit values) and O, each aligned to its width:
+  //   D=64,  N=128: S [0,128)  P [128,192)  O [192,256)
+  //   D=128, N=64:  O [0,128)  S [128,192)  P [192,224)
+  static constexpr uint32_t kWgCols = 256;
+  static constexpr uint32_t kTmemS = D == 64 ? 0 : 128;
+  static constexpr uint32_t kTmemP = kTmemS + N;
+  static constexpr uint32_t kTmemO = D == 64 ? 192 : 0;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kBoxes = (N / kBoxTokens) * kDH;  // per K (and per V) tile
   static_assert(kBoxes <= 32, "one TMA box per producer lane");
-  static_assert(kTmemO + 2 * D <= kTmemCols, "TMEM budget");
+  static_assert(kTmemP + N / 2 <= kWgCols && kTmemO + D <= kWgCols &&
+                (kTmemO + D <= kTmemS || kTmemO >= kTmemP + N / 2), "TMEM layout");
+  static_assert(N % 32 == 0 && N <= 128, "S row loads in 32-column pieces");
 };
 
 struct TcParams {
@@ -196,10 +207,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* q_empty = q_full + QB;
   uint64_t* kv_full = q_empty + QB;
   uint64_t* kv_empty = kv_full + ST;
-  uint64_t* s_full = kv_empty + ST;   // [2], MMA commit
-  uint64_t* p_full = s_full + 2;      // [2], 128 softmax arrivals
-  uint64_t* o_ready = p_full + 2;     // [2], MMA commit after an item's last P V
-  uint64_t* o_empty = o_ready + 2;    // [2], 128 arrivals once O is read out
+  uint64_t* s_full = kv_empty + ST;   // [2], MMA commit after S_w
+  uint64_t* s_free = s_full + 2;      // [2], 128 arrivals: S_w read into registers
+  uint64_t* p_full = s_free + 2;      // [2], 128 arrivals: P_w in TMEM (and O_w rescaled)
+  uint64_t* pv_done = p_full + 2;     // [2], MMA commit after P_w V
+  uint64_t* o_empty = pv_done + 2;    // [2], 128 arrivals once an item's O is read out
   uint64_t* mma_done = o_empty + 2;
   uint64_t* item_full = mma_done + 1;          // [kRing], producer publishes an index
   uint64_t* item_empty = item_full + L::kRing;  // [kRing], 9 consumer warps took it
@@ -220,8 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_ready[i], 1);
+      mbar_init(&pv_done[i], 1);
       mbar_init(&o_empty[i], 128);
     }
     mbar_init(mma_done, 1);
@@ -362,7 +375,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const uint32_t q_lo = tc::desc_lo(sbase + L::kOffQ, 16);
       const uint32_t k_lo = tc::desc_lo(sbase + L::kOffK, 16);
       const uint32_t v_lo = tc::desc_lo(sbase + L::kOffV, N * 128);
-      const uint32_t p_lo = tc::desc_lo(sbase + L::kOffP, 16);
       uint32_t li = 0, g = 0;
       bool ok = true;
       // O_w += P_w V(stage) for the tile whose softmax was the t-th of group w.
@@ -371,20 +383,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         if (ok && first_of_item && li > 0) ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
         if (!ok) return;
         tc::fence_after_sync();
-        // One add per operand per MMA: offsets are compile-time (>> 4).
-        const uint32_t a0 = p_lo + w * (L::kPTile >> 4);
+        // P_w is read from TMEM (8 columns per K=16 step), V from shared
+        // memory; one add per MMA (compile-time offsets).
+        const uint32_t a0 = tmem + w * L::kWgCols + L::kTmemP;
         const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
-        const uint32_t d = tmem + L::kTmemO + w * D;
-        tc::mma_ss_words(d, a0, b0, kHi, idesc_o, accumulate ? 1u : 0u);
+        const uint32_t d = tmem + w * L::kWgCols + L::kTmemO;
+        tc::mma_ts_words(d, a0, b0, kHi, idesc_o, accumulate ? 1u : 0u);
 #pragma unroll
         for (int kk = 1; kk < N / 16; ++kk)
-          tc::mma_ss_words(d, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4), b0 + ((kk * 2048) >> 4), kHi,
-                           idesc_o, 1u);
+          tc::mma_ts_words(d, a0 + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o, 1u);
+        tc::commit(&pv_done[w]);
       };
       auto issue_s = [&](int w, int qb, int stage) {
         const uint32_t a0 = q_lo + (qb * 2 + w) * (L::kQTile >> 4);
         const uint32_t b0 = k_lo + stage * (L::kKVTile >> 4);
-        const uint32_t d = tmem + L::kTmemS + w * N;
+        const uint32_t d = tmem + w * L::kWgCols + L::kTmemS;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           tc::mma_ss_words(d, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4),
@@ -407,18 +420,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           if (ok && *abort_flag) ok = false;
           if (!ok) break;
           tc::fence_after_sync();
+          // S_w(g) as soon as the softmax has read S_w(g-1) into registers,
+          // then the P V of the previous tile once its P is in TMEM.
           for (int w = 0; w < 2 && ok; ++w) {
-            if (j > 0) issue_pv(w, g - 1, (g - 1) % ST, j > 1, j == 1);
-            if (ok) issue_s(w, qb, st);
+            if (g > 0) ok = mbar_wait(&s_free[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+            if (!ok) break;
+            tc::fence_after_sync();
+            issue_s(w, qb, st);
           }
-          if (ok && j > 0) tc::commit(&kv_empty[(g - 1) % ST]);
+          if (ok && j > 0) {
+            for (int w = 0; w < 2 && ok; ++w) issue_pv(w, g - 1, (g - 1) % ST, j > 1, j == 1);
+            if (ok) tc::commit(&kv_empty[(g - 1) % ST]);
+          }
         }
         if (!ok) break;
-        // Last P V of the item, then release its Q buffer and O.
-        for (int w = 0; w < 2 && ok; ++w) {
-          issue_pv(w, g - 1, (g - 1) % ST, it.ntiles > 1, it.ntiles == 1);
-          if (ok) tc::commit(&o_ready[w]);
-        }
+        // Last P V of the item, then release its K/V stage and Q buffer.
+        for (int w = 0; w < 2 && ok; ++w) issue_pv(w, g - 1, (g - 1) % ST, it.ntiles > 1, it.ntiles == 1);
         if (!ok) break;
         tc::commit(&kv_empty[(g - 1) % ST]);
         tc::commit(&q_empty[qb]);
@@ -436,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const int w = warp >> 2;                 // M-tile of this group
     const int quarter = warp & 3;            // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;       // row of the M-tile = TMEM lane
-    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t wg_addr = tmem + ((uint32_t)(quarter * 32) << 16) + w * L::kWgCols;
     const int pl = r / p.G, hj = r - (r / p.G) * p.G;
     const bool row_in_tile = r < p.G * p.P;
     uint32_t li = 0, t = 0;
@@ -464,8 +481,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         tc::fence_after_sync();
         uint32_t su[N];  // S row as raw bits
 #pragma unroll
-        for (int c = 0; c < N / 32; ++c) tc::tmem_ld32(lane_addr + L::kTmemS + w * N + c * 32, su + c * 32);
+        for (int c = 0; c < N / 32; ++c) tc::tmem_ld32(wg_addr + L::kTmemS + c * 32, su + c * 32);
         tc::tmem_wait_ld();
+        tc::fence_before_sync();
+        mbar_arrive(&s_free[w]);  // S_w may now be overwritten by the next tile's S
         if (j >= nfull) {
           const int lim = Lr - j * N;  // keep keys k <= lim
 #pragma unroll
@@ -476,23 +495,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
         for (int q = 0; q < N / 2; ++q) mx4[q & 3] = fmax3(mx4[q & 3], SV(2 * q), SV(2 * q + 1));
         const float mx = fmax3(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3], mx4[3]) * p.scale_log2;
+        // The P V of the previous tile has finished: O_w is current and P_w
+        // free.  (It also keeps this group at most one p_full phase ahead of
+        // the MMA warp, which waits on parity.)
+        if (t >= 1) {
+          ok = mbar_wait(&pv_done[w], (t - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc::fence_after_sync();
+        }
         if (j == 0) {
           m_run = mx;  // key 0 is always visible: finite
         } else {
           const float m_new = fmaxf(m_run, mx);
           const bool need = m_new > m_run + kRescaleLog2;
           if (__any_sync(0xffffffffu, need)) {
-            // O_w holds P V up to tile j-1 (complete: the commit behind
-            // s_full covered it).  Scale the rows that need it in TMEM.
+            // O_w holds P V up to tile j-1: scale the rows that need it.
             const float alpha = need ? fast_exp2(m_run - m_new) : 1.f;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
               uint32_t ov[32];
-              tc::tmem_ld32(lane_addr + L::kTmemO + w * D + c * 32, ov);
+              tc::tmem_ld32(wg_addr + L::kTmemO + c * 32, ov);
               tc::tmem_wait_ld();
 #pragma unroll
               for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * alpha);
-              tc::tmem_st32(lane_addr + L::kTmemO + w * D + c * 32, ov);
+              tc::tmem_st32(wg_addr + L::kTmemO + c * 32, ov);
             }
             tc::tmem_wait_st();
             if (need) {
@@ -523,10 +550,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 negm2 = make_float2(-m_run, -m_run);
         float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        uint8_t* prow = smem + L::kOffP + w * L::kPTile + r * 128;
+        uint32_t pk[N / 2];  // P row, two 16-bit values per 32-bit TMEM column
 #pragma unroll
         for (int c = 0; c < N / 8; ++c) {
-          uint32_t packed[4];
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
             const int q = c * 4 + h;
@@ -539,23 +565,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
               e.y = fast_exp2(x.y);
             }
             sum2[h] = __fadd2_rn(sum2[h], e);
-            packed[h] = pack2<T>(e.x, e.y);
+            pk[q] = pack2<T>(e.x, e.y);
           }
-          const int4 v = make_int4(static_cast<int>(packed[0]), static_cast<int>(packed[1]),
-                                   static_cast<int>(packed[2]), static_cast<int>(packed[3]));
-          *reinterpret_cast<int4*>(prow + (c >> 3) * L::kSlab + (((c & 7) ^ (r & 7)) << 4)) = v;
         }
+        const uint32_t p_addr = wg_addr + L::kTmemP;
+#pragma unroll
+        for (int c = 0; c + 32 <= N / 2; c += 32) tc::tmem_st32(p_addr + c, pk + c);
+        if ((N / 2) % 32) tc::tmem_st16(p_addr + (N / 2) / 32 * 32, pk + (N / 2) / 32 * 32);
+        tc::tmem_wait_st();
 #undef SV
         const float2 s01 = __fadd2_rn(sum2[0], sum2[1]), s23 = __fadd2_rn(sum2[2], sum2[3]);
         const float2 s0123 = __fadd2_rn(s01, s23);
         l += s0123.x + s0123.y;
-        fence_proxy_async_smem();
+        fence_proxy_async_smem();  // V rows zeroed above (generic proxy) -> MMA reads
         tc::fence_before_sync();
         mbar_arrive(&p_full[w]);
       }
       if (!ok) break;
       // Epilogue: the item's last P V has landed in O_w.
-      ok = mbar_wait(&o_ready[w], li & 1, p.status, PA_DEVICE_TIMEOUT_MMA) && !*abort_flag;
+      ok = mbar_wait(&pv_done[w], (t - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA) && !*abort_flag;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc::fence_after_sync();
@@ -565,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t ov[32];
-        tc::tmem_ld32(lane_addr + L::kTmemO + w * D + c * 32, ov);
+        tc::tmem_ld32(wg_addr + L::kTmemO + c * 32, ov);
         tc::tmem_wait_ld();
         if (live) {
 #pragma unroll
