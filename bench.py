@@ -12,8 +12,10 @@ BF16.  One step = for every layer, the batched KV write of the new token
 (model/qwen2.py:608-621).  Per step the KV pools stream ~1.66 GB, far above the
 126 MB L2, so no flush is needed between steps.
 
-Multi-GPU: one process per GPU (torchrun), requests sharded by rank with no
-communication (weak scaling: every rank decodes its own batch of 64).
+Multi-GPU: one process per GPU (torchrun).  The global batch is 64 * N
+requests drawn once; every rank keeps its shard (longest-first on context
+length, so ranks stream equal KV) in its own pool and decodes it with no
+communication (weak scaling: ~64 requests per GPU).
 
 The JSON line: ``value`` = whole-job algorithmic KV bytes per second (device
 time, inputs resident); ``e2e`` = the same metric through the public API with
@@ -93,21 +95,31 @@ def bf16_peak():
     return _peak("bf16_tflops", FALLBACK_BF16_TFLOPS)
 
 
-def make_metadata(seed: int):
-    """Seeded contexts / block tables / slots for one rank's batch (numpy)."""
+def make_metadata(seed: int, world: int = 1, rank: int = 0):
+    """Seeded contexts / block tables / slots for one rank (numpy).
+
+    The global batch is BATCH * world requests; every rank draws the same
+    contexts and keeps its request shard (LPT on context length,
+    mini_llm_runtime_b200.sharding), with a pool of its shard's blocks + 10 %.
+    world = 1 is exactly the config-2 draw."""
+    from mini_llm_runtime_b200.sharding import decode_cost, shard_requests
+
     rng = np.random.default_rng(seed)
-    ctx = rng.integers(CTX_LO, CTX_HI + 1, size=BATCH).astype(np.int64)
+    ctx = rng.integers(CTX_LO, CTX_HI + 1, size=BATCH * world).astype(np.int64)
+    if world > 1:
+        ctx = ctx[shard_requests([decode_cost(c) for c in ctx], world)[rank].requests]
+    n = len(ctx)
     need = (ctx + BS - 1) // BS
     nb = int(math.ceil(need.sum() * 1.1))
     perm = rng.permutation(nb)
     width = int(need.max())
-    tables = np.full((BATCH, width), -1, dtype=np.int64)
+    tables = np.full((n, width), -1, dtype=np.int64)
     cur = 0
-    for b in range(BATCH):
+    for b in range(n):
         tables[b, : need[b]] = perm[cur : cur + need[b]]
         cur += need[b]
     pos = ctx - 1
-    slots = tables[np.arange(BATCH), pos // BS] * BS + pos % BS
+    slots = tables[np.arange(n), pos // BS] * BS + pos % BS
     return ctx, tables, slots, nb
 
 
@@ -117,9 +129,10 @@ def algorithmic_bytes(ctx: np.ndarray) -> dict:
     B * Hq * D * 2 B each, block-table reads sum(ceil(ctx/16)) * 8 B, and the
     new-token KV write B * Hkv * D * 2 B * 2."""
     kv = int(ctx.sum()) * HKV * D * 2 * 2
-    qo = 2 * BATCH * HQ * D * 2
+    n = len(ctx)
+    qo = 2 * n * HQ * D * 2
     table = int(((ctx + BS - 1) // BS).sum()) * 8
-    scatter = BATCH * HKV * D * 2 * 2
+    scatter = n * HKV * D * 2 * 2
     return {"kv": kv, "decode": kv + qo + table, "layer": kv + qo + table + scatter}
 
 
@@ -138,11 +151,11 @@ class ClockSampler:
     def start(self):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
+            self._out = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu_index), "-f", self.path],
-                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu_index)],
+                stdout=self._out, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
 
@@ -154,6 +167,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        self._out.close()
         rows = []
         try:
             for line in Path(self.path).read_text().splitlines():
@@ -406,19 +420,20 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------------------
 
 
-def build_rank_workload(rank: int, device):
+def build_rank_workload(rank: int, world: int, device):
     from mini_llm_runtime_b200 import PagedKVCache
 
-    ctx, tables, slots, nb = make_metadata(1000 + rank)
+    ctx, tables, slots, nb = make_metadata(1000, world, rank)
+    n = len(ctx)
     cache = PagedKVCache(LAYERS, nb, BS, HKV, D, dtype=torch.bfloat16, device=device)
     g = torch.Generator(device=device).manual_seed(2000 + rank)
     cache.k_cache.normal_(generator=g)
     cache.v_cache.normal_(generator=g)
     gen = torch.Generator().manual_seed(3000 + rank)
     inputs = {
-        "q": torch.randn(LAYERS, BATCH, HQ, D, generator=gen).to(torch.bfloat16),
-        "new_k": torch.randn(LAYERS, BATCH, HKV, D, generator=gen).to(torch.bfloat16),
-        "new_v": torch.randn(LAYERS, BATCH, HKV, D, generator=gen).to(torch.bfloat16),
+        "q": torch.randn(LAYERS, n, HQ, D, generator=gen).to(torch.bfloat16),
+        "new_k": torch.randn(LAYERS, n, HKV, D, generator=gen).to(torch.bfloat16),
+        "new_v": torch.randn(LAYERS, n, HKV, D, generator=gen).to(torch.bfloat16),
         "slot_mapping": torch.tensor(slots),
         "block_tables": torch.tensor(tables),
         "context_lens": torch.tensor(ctx),
@@ -455,7 +470,7 @@ def main():
     from mini_llm_runtime_b200 import PagedDecodeGraph, _lib
 
     _lib.load()
-    w = build_rank_workload(rank, device)
+    w = build_rank_workload(rank, world, device)
     nbytes = algorithmic_bytes(w["ctx"])
     warmup = max(args.warmup, 3)
 
@@ -471,7 +486,8 @@ def main():
         dist.all_reduce(t, op=op)
         return float(t.item())
 
-    mk = lambda **kw: PagedDecodeGraph(w["cache"], BATCH, w["width"], HQ, range(LAYERS), **kw)  # noqa: E731
+    batch = len(w["ctx"])
+    mk = lambda **kw: PagedDecodeGraph(w["cache"], batch, w["width"], HQ, range(LAYERS), **kw)  # noqa: E731
 
     # ---- device-resident step: KV write + decode for 24 layers, one graph --
     g_dev = mk(host_io=False)
@@ -479,8 +495,16 @@ def main():
     g_dev.validate({k: w["inputs"][k] for k in ("context_lens", "block_tables", "slot_mapping")})
     for _ in range(warmup):
         g_dev.run(validate=False)
+    # nvidia-smi samples every 100 ms: keep the same step running (untimed)
+    # for about a second so the samples see the load the timed region runs
+    # under, then time K steps straight after.
     sampler = ClockSampler(physical_gpu_index(local_rank))
     sampler.start()
+    soak_end = time.perf_counter() + 1.0
+    while time.perf_counter() < soak_end:
+        for _ in range(50):
+            g_dev.run(validate=False)
+        torch.cuda.synchronize()
     barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -525,7 +549,7 @@ def main():
     e2e_ms = reduce(e0.elapsed_time(e1) / args.steps, dist.ReduceOp.MAX if world > 1 else None)
 
     total_kv = reduce(nbytes["kv"] * LAYERS, dist.ReduceOp.SUM if world > 1 else None)
-    tokens = reduce(BATCH, dist.ReduceOp.SUM if world > 1 else None)
+    tokens = reduce(batch, dist.ReduceOp.SUM if world > 1 else None)
     value = total_kv / (ms_step * 1e-3) / 1e9
     e2e_value = total_kv / (e2e_ms * 1e-3) / 1e9
 
@@ -567,9 +591,11 @@ def main():
             "data": "synthetic",
             "config": {
                 "workload": "config2: bf16 batched paged decode (KV write + decode per layer), 24 layers, "
-                            "14/2 heads, D64, bs16, batch 64 per GPU, ctx U[128,4096], pool = blocks*1.1",
+                            "14/2 heads, D64, bs16, global batch 64*N sharded by request (LPT on ctx), "
+                            "ctx U[128,4096], pool = blocks*1.1 per rank",
                 "global_batch": BATCH * world,
                 "parallelism": f"request-sharded dp{world}, no communication",
+                "rank0_batch": batch,
                 "l2": "inputs larger than L2 (1.66 GB of KV streamed per step per GPU), no flush",
                 "launch": "one CUDA graph per step (48 kernel nodes)",
             },
