@@ -791,7 +791,10 @@ int current_device() {
 #endif
 constexpr int kFlatNW64 = PA_FLAT_NW64, kFlatST64 = PA_FLAT_ST64;
 constexpr int kFlatNW128 = 2, kFlatST128 = 4;
-constexpr int kFlatCtasPerSm = 2;
+#ifndef PA_FLAT_CTAS
+#define PA_FLAT_CTAS 2
+#endif
+constexpr int kFlatCtasPerSm = PA_FLAT_CTAS;
 constexpr int flat_nw(int D) { return D == 64 ? kFlatNW64 : kFlatNW128; }
 constexpr int kSplitNW = 4, kSplitST = 4;
 

@@ -32,9 +32,12 @@ import torch
 
 from . import _lib
 from .paged_kv_cache import PagedKVCache
+from .qwen2_attention import check_decode_metadata
 
 
 class PagedDecodeGraph:
+    COPY_CHUNK_LAYERS = 4  # layers per host<->device copy chunk (host I/O mode)
+
     def __init__(
         self,
         cache: PagedKVCache,
@@ -89,19 +92,45 @@ class PagedDecodeGraph:
         self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
         self.graph = None
         self._stream = torch.cuda.Stream(dev)
+        self._h2d = torch.cuda.Stream(dev)
+        self._d2h = torch.cuda.Stream(dev)
         self._capture()
 
     # -- step body --------------------------------------------------------------
     def _body(self, stream: int, warm: bool = False) -> None:
         """Enqueue one step.  ``warm`` = eager first pass before capture: no
-        copies and no KV writes (it must not modify the cache), decode only."""
+        copies and no KV writes (it must not modify the cache), decode only.
+
+        With host I/O the per-layer inputs travel in chunks of
+        ``COPY_CHUNK_LAYERS`` layers: the metadata and the first chunk on the
+        step's stream, the others on a side stream while the first layers
+        run, and each chunk's outputs go back on another side stream as soon
+        as its layers finish, so the copy engines work under the kernels."""
         lib, c = self._lib, self.cache
         B, H, D, HKV, bs = self.batch, self.hq, c.head_dim, c.num_kv_heads, c.block_size
-        if self.host_io and not warm:
-            for k, d in self._dev_inputs.items():
-                d.copy_(self.host_inputs[k], non_blocking=True)
+        io = self.host_io and not warm
+        main = torch.cuda.current_stream(self.device)
+        L, CH = len(self.layers), self.COPY_CHUNK_LAYERS
+        chunks = [(a, min(a + CH, L)) for a in range(0, L, CH)]
+        ready = {}
+        if io:
+            for k in ("slot_mapping", "block_tables", "context_lens"):
+                self._dev_inputs[k].copy_(self.host_inputs[k], non_blocking=True)
+            self._h2d.wait_stream(main)
+            for ci, (a, b) in enumerate(chunks):
+                ctx = torch.cuda.stream(main if ci == 0 else self._h2d)
+                with ctx:
+                    for k in ("q", "new_k", "new_v"):
+                        self._dev_inputs[k][a:b].copy_(self.host_inputs[k][a:b], non_blocking=True)
+                    if ci > 0:
+                        ev = torch.cuda.Event()
+                        ev.record(self._h2d)
+                        ready[a] = ev
+            self._d2h.wait_stream(main)
         num_slots = c.num_blocks * bs
         for i, layer in enumerate(self.layers):
+            if i in ready:
+                main.wait_event(ready[i])
             nk, nv, q, o = self.new_k[i], self.new_v[i], self.q[i], self.out[i]
             kp, vp = c.k_cache[layer], c.v_cache[layer]
             if self.write_kv and not warm:
@@ -116,8 +145,15 @@ class PagedDecodeGraph:
                 o.data_ptr(), o.stride(0), o.stride(1), B, H, self.scale, self._code, self.partition_tokens,
                 self.workspace.data_ptr(), self.workspace.numel(), stream)
             _lib.check(st, "pa_paged_decode")
-        if self.host_io and not warm:
-            self.host_output.copy_(self.out, non_blocking=True)
+            if io and any(i == b - 1 for _, b in chunks):
+                a = max(a for a, b in chunks if b == i + 1)
+                done = torch.cuda.Event()
+                done.record(main)
+                self._d2h.wait_event(done)
+                with torch.cuda.stream(self._d2h):
+                    self.host_output[a:i + 1].copy_(self.out[a:i + 1], non_blocking=True)
+        if io:
+            main.wait_stream(self._d2h)
 
     def _capture(self) -> None:
         # One eager decode-only pass on a side stream (first-use kernel
@@ -136,24 +172,8 @@ class PagedDecodeGraph:
     # -- host-side metadata checks (model/qwen2.py:580-602, paged_kv_cache.py:228-239)
     def validate(self, inputs: dict | None = None) -> None:
         src = self.host_inputs if inputs is None else inputs
-        c = self.cache
-        lens = src["context_lens"].numpy()
-        tables = src["block_tables"].numpy()
-        slots = src["slot_mapping"].numpy()
-        if np.any(lens <= 0):
-            raise ValueError("context_lens must be greater than 0")
-        need = (lens + c.block_size - 1) // c.block_size
-        if np.any(need > tables.shape[1]):
-            raise ValueError("block_tables have insufficient blocks for context_lens")
-        used = np.arange(tables.shape[1])[None, :] < need[:, None]
-        if np.any(used & ((tables < 0) | (tables >= c.num_blocks))):
-            raise ValueError("block_tables contain an invalid physical block")
-        pos = lens - 1
-        expected = tables[np.arange(len(lens)), pos // c.block_size] * c.block_size + pos % c.block_size
-        if np.any(slots != expected):
-            raise ValueError("slot_mapping must match block_tables and positions")
-        if np.unique(slots).size != slots.size:
-            raise ValueError("decode requests must use distinct write slots")
+        check_decode_metadata(src["context_lens"].numpy(), src["block_tables"].numpy(), src["slot_mapping"].numpy(),
+                              None, self.cache.block_size, self.cache.num_blocks)
 
     def run(self, validate: bool = True) -> None:
         """Validate the staged metadata on the host and replay the step on the

@@ -204,14 +204,16 @@ def test_tiny_batches_leave_ctas_idle(cuda_device):
         check(out, oracle_decode(case), torch.float16)
 
 
-def test_decode_graph_step_matches_eager(cuda_device):
+@pytest.mark.parametrize("layers", [3, 9])
+def test_decode_graph_step_matches_eager(cuda_device, layers):
     """PagedDecodeGraph (CUDA graph of KV write + decode per layer, with
-    pinned host I/O) gives the same cache and outputs as eager calls."""
+    pinned host I/O copied in layer chunks that overlap the kernels) gives
+    the same cache and outputs as eager calls, step after step."""
     from mini_llm_runtime_b200 import PagedDecodeGraph
 
     torch.manual_seed(3)
     ctx = [37, 600, 1025, 64]
-    layers, hq, hkv, d, bs = 3, 14, 2, 64, 16
+    hq, hkv, d, bs = 14, 2, 64, 16
     need = [(c + bs - 1) // bs for c in ctx]
     nb = sum(need) + 5
     perm = torch.randperm(nb).tolist()
@@ -233,15 +235,19 @@ def test_decode_graph_step_matches_eager(cuda_device):
     hi["block_tables"].copy_(torch.tensor(tables))
     hi["context_lens"].copy_(torch.tensor(ctx))
     hi["slot_mapping"].copy_(torch.tensor([tables[b][(c - 1) // bs] * bs + (c - 1) % bs for b, c in enumerate(ctx)]))
-    g.run()
-    g.synchronize()
-    dv = {k: v.to(cuda_device) for k, v in hi.items()}
-    for layer in range(layers):
-        ref.write_slots(dv["slot_mapping"], dv["new_k"][layer], dv["new_v"][layer], layer)
-        exp = paged_attention_decode_batch_parallel(dv["q"][layer], ref.k_cache[layer], ref.v_cache[layer],
-                                                    dv["block_tables"], dv["context_lens"], bs)
-        assert torch.equal(g.host_output[layer], exp.cpu())
-    assert torch.equal(cache.k_cache.view(torch.int16), ref.k_cache.view(torch.int16))
+    for step in range(2):
+        if step:
+            hi["q"].copy_(torch.randn(hi["q"].shape).to(torch.bfloat16))
+            hi["new_k"].copy_(torch.randn(hi["new_k"].shape).to(torch.bfloat16))
+        g.run()
+        g.synchronize()
+        dv = {k: v.to(cuda_device) for k, v in hi.items()}
+        for layer in range(layers):
+            ref.write_slots(dv["slot_mapping"], dv["new_k"][layer], dv["new_v"][layer], layer)
+            exp = paged_attention_decode_batch_parallel(dv["q"][layer], ref.k_cache[layer], ref.v_cache[layer],
+                                                        dv["block_tables"], dv["context_lens"], bs)
+            assert torch.equal(g.host_output[layer], exp.cpu())
+        assert torch.equal(cache.k_cache.view(torch.int16), ref.k_cache.view(torch.int16))
     with pytest.raises(ValueError, match="slot_mapping must match"):
         hi["slot_mapping"][0] += 1
         g.run()
