@@ -495,15 +495,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
         for (int q = 0; q < N / 2; ++q) mx4[q & 3] = fmax3(mx4[q & 3], SV(2 * q), SV(2 * q + 1));
         const float mx = fmax3(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3], mx4[3]) * p.scale_log2;
-        // The P V of the previous tile has finished: O_w is current and P_w
-        // free.  (It also keeps this group at most one p_full phase ahead of
-        // the MMA warp, which waits on parity.)
-        if (t >= 1) {
-          ok = mbar_wait(&pv_done[w], (t - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc::fence_after_sync();
-        }
+        // The P V of the previous tile must finish before O_w is rescaled or
+        // P_w overwritten; wait for it only where needed, so the exponentials
+        // below overlap it.  (Waiting before every P store also keeps this
+        // group at most one p_full phase ahead of the MMA warp.)
+        bool pv_waited = t == 0;
+        auto wait_pv = [&]() {
+          if (pv_waited) return true;
+          pv_waited = true;
+          bool w_ok = mbar_wait(&pv_done[w], (t - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+          w_ok = __all_sync(0xffffffffu, w_ok);
+          if (w_ok) tc::fence_after_sync();
+          return w_ok;
+        };
         if (j == 0) {
           m_run = mx;  // key 0 is always visible: finite
         } else {
@@ -511,6 +515,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           const bool need = m_new > m_run + kRescaleLog2;
           if (__any_sync(0xffffffffu, need)) {
             // O_w holds P V up to tile j-1: scale the rows that need it.
+            ok = wait_pv();
+            if (!ok) break;
             const float alpha = need ? fast_exp2(m_run - m_new) : 1.f;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
@@ -568,6 +574,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             pk[q] = pack2<T>(e.x, e.y);
           }
         }
+        ok = wait_pv();
+        if (!ok) break;
         const uint32_t p_addr = wg_addr + L::kTmemP;
 #pragma unroll
         for (int c = 0; c + 32 <= N / 2; c += 32) tc::tmem_st32(p_addr + c, pk + c);

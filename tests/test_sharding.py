@@ -102,3 +102,24 @@ def test_two_gloo_ranks_decode_their_shards(tmp_path):
     path = str(tmp_path / "result")
     mp.start_processes(_rank_main, args=(2, port, path), nprocs=2, join=True, start_method="spawn")
     assert open(path).read() == "ok"
+
+
+def test_bench_shards_cover_the_global_batch():
+    """bench.py's per-rank metadata: every rank's contexts are its shard of
+    the same global draw, pools hold exactly the shard's blocks + 10 %, and
+    the N = 1 draw is the config-2 workload."""
+    import bench
+
+    full, _, _, _ = bench.make_metadata(1000)
+    assert len(full) == bench.BATCH
+    for world in (2, 4):
+        glob = np.random.default_rng(1000).integers(bench.CTX_LO, bench.CTX_HI + 1, size=bench.BATCH * world)
+        parts = [bench.make_metadata(1000, world, r) for r in range(world)]
+        got = np.sort(np.concatenate([p[0] for p in parts]))
+        assert np.array_equal(got, np.sort(glob))
+        for ctx, tables, slots, nb in parts:
+            need = (ctx + bench.BS - 1) // bench.BS
+            used = tables[tables >= 0]
+            assert len(np.unique(used)) == need.sum() and used.max() < nb
+            pos = ctx - 1
+            assert np.array_equal(slots, tables[np.arange(len(ctx)), pos // bench.BS] * bench.BS + pos % bench.BS)
