@@ -135,6 +135,34 @@ PA_API int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const void
                     int partition_tokens, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * KV write of the new token fused with batched decode: the effect of
+ * pa_kv_scatter(new_k, new_v -> slot_mapping) followed by pa_paged_decode,
+ * in one launch where it can be fused.  Replaces the pair the reference runs
+ * per layer, PagedKVCache.write_slots (runtime/paged_kv_cache.py:194-249)
+ * then paged_attention_decode_batch_parallel
+ * (kernels/reference/paged_attention.py:178-254), as called by
+ * Qwen2Attention.forward_decode_batch_with_cache (model/qwen2.py:608-621).
+ *
+ * new_k, new_v : [batch, num_kv_heads, head_dim], contiguous, pool dtype
+ * slot_mapping : [batch] int64; slot_mapping[b] must be the slot of
+ *                position context_lens[b] - 1 of sequence b's block table
+ *                (the reference checks this, qwen2.py:594-600) and the
+ *                slots distinct; other sequences must not map that slot
+ *                into their context.
+ * The decode kernel patches the new token's rows into the K/V it stages and
+ * stores them to the pools; the output and the pools end up equal to the
+ * unfused pair (bit for bit).  Falls back to the two calls where the fused
+ * kernel does not apply (F32, odd head_dim or block size, misalignment).
+ * Workspace as for pa_paged_decode with partition_tokens = 0.
+ */
+PA_API int pa_paged_decode_write(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k, const void* new_v,
+                          const int64_t* slot_mapping, void* k_pool_layer, void* v_pool_layer, int64_t num_blocks,
+                          int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
+                          int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
+                          int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/*
  * pa_paged_decode without a caller-supplied workspace: for callers that
  * cannot allocate device memory (a host runtime that owns every device byte
  * through its own arena, an FFI host with no device allocator, a serving

@@ -12,6 +12,7 @@ from .paged_attention import (
     paged_attention_decode_split_kv,
     paged_attention_prefill_chunk_tiled,
     paged_attention_prefill_varlen,
+    paged_decode_with_kv_write,
 )
 from .decode_graph import PagedDecodeGraph
 from .paged_kv_cache import PagedKVCache
@@ -27,4 +28,5 @@ __all__ = [
     "paged_attention_decode_split_kv",
     "paged_attention_prefill_chunk_tiled",
     "paged_attention_prefill_varlen",
+    "paged_decode_with_kv_write",
 ]

@@ -45,6 +45,12 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i64, _i64,
          _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _f32, _i32, _i32, _c_void_p, _size, _c_void_p],
     ),
+    "pa_paged_decode_write": (
+        _i32,
+        [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32,
+         _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _f32, _i32, _c_void_p, _size,
+         _c_void_p],
+    ),
     "pa_paged_decode_noalloc": (
         _i32,
         [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32, _c_void_p, _i64, _i64,

@@ -256,6 +256,15 @@ struct FlatParams {
   float* part_o;   // [W][2][16][D]   unnormalised O of the same
   int* prefix;     // [B + 1] per-sequence sub-block prefix sums (for the combine kernel)
   int* status;
+  // Fused KV write (all null when the new token is already in the pools):
+  // the new token's K/V rows [B, Hkv, D] (contiguous, pool dtype) replace the
+  // pool rows in the staged sub-block and are stored to slots[b] of the pools.
+  const void* new_k;
+  const void* new_v;
+  const int64_t* slots;
+  void* k_pool;
+  void* v_pool;
+  int64_t num_slots;
 };
 
 // Segment cursor over the flattened sub-block index space.
@@ -459,6 +468,31 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
           vb[u] = kb[u] + C::kColTiles * kTileBytes;
           const int64_t sub = lo + j - pc.start;
           valid[u] = static_cast<int>(min((int64_t)kSub, ctx - sub * kSub));
+          if (p.new_k != nullptr && (sub + 1) * kSub >= ctx) {
+            // Fused KV write: the sub-block holding the new token (position
+            // ctx - 1) gets its K/V rows from new_k / new_v in place of the
+            // pool's, and the head-tile-0 warp stores them to the pools.
+            // Lane i moves one 16-byte chunk: K then V, 64-column tiles,
+            // 8 chunks per 128-byte row (the TMA's 128-byte swizzle).
+            const int r = static_cast<int>(ctx - 1 - sub * kSub);
+            constexpr int kChunks = 2 * C::kColTiles * 8;
+            if (lane < kChunks) {
+              const int kv = lane / (C::kColTiles * 8), rem = lane - kv * (C::kColTiles * 8);
+              const int ct = rem >> 3, c = rem & 7;
+              const int64_t src = ((int64_t)b * p.Hkv + kvh) * D + ct * 64 + c * 8;
+              const int4 val = __ldg(reinterpret_cast<const int4*>(
+                  reinterpret_cast<const T*>(kv ? p.new_v : p.new_k) + src));
+              uint8_t* dst = ring + stage * C::kStageBytes + (kv * C::kColTiles + ct) * kTileBytes + r * 128 +
+                             ((c ^ (r & 7)) << 4);
+              *reinterpret_cast<int4*>(dst) = val;
+              const int64_t slot = p.slots[b];
+              if (ht == 0 && slot >= 0 && slot < p.num_slots)
+                *reinterpret_cast<int4*>(reinterpret_cast<T*>(kv ? p.v_pool : p.k_pool) +
+                                         (slot * p.Hkv + kvh) * D + ct * 64 + c * 8) = val;
+              fence_proxy_async_smem();  // before the stage is refilled by TMA
+            }
+            __syncwarp();
+          }
         }
       }
       if (n == 2) ws.template consume<2>(kb, vb, valid, p.scale_log2, lane);
@@ -922,13 +956,74 @@ extern "C" size_t pa_decode_workspace_bytes(int batch, int num_kv_heads, int num
       .ws_bytes;
 }
 
+namespace pa {
+namespace {
+
+// The new token's K/V for a fused write (see pa_paged_decode_write).
+struct FusedWrite {
+  const void* new_k;
+  const void* new_v;
+  const int64_t* slots;
+};
+
+int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_layer, const void* v_pool_layer,
+                int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
+                int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
+                int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
+                void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused);
+
+}  // namespace
+}  // namespace pa
+
 extern "C" int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_layer,
                                const void* v_pool_layer, int64_t num_blocks, int block_size, int num_kv_heads,
                                int head_dim, const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
                                const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
                                int num_q_heads, float scale, int dtype, int partition_tokens, void* workspace,
                                size_t workspace_bytes, void* stream) {
+  return pa::decode_impl(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads, head_dim,
+                         block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch, num_q_heads, scale,
+                         dtype, partition_tokens, workspace, workspace_bytes, stream, nullptr, nullptr);
+}
+
+extern "C" int pa_paged_decode_write(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k,
+                                     const void* new_v, const int64_t* slot_mapping, void* k_pool_layer,
+                                     void* v_pool_layer, int64_t num_blocks, int block_size, int num_kv_heads,
+                                     int head_dim, const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
+                                     const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
+                                     int num_q_heads, float scale, int dtype, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
   using namespace pa;
+  if (batch < 0) return PA_ERR_INVALID;
+  if (batch == 0) return PA_OK;
+  if (new_k == nullptr || new_v == nullptr || slot_mapping == nullptr) return PA_ERR_INVALID;
+  const bool aligned = !((reinterpret_cast<uintptr_t>(new_k) | reinterpret_cast<uintptr_t>(new_v)) & 15);
+  FusedWrite fw{new_k, new_v, slot_mapping};
+  bool fused = false;
+  if (aligned) {
+    const int r = decode_impl(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads,
+                              head_dim, block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch,
+                              num_q_heads, scale, dtype, 0, workspace, workspace_bytes, stream, &fw, &fused);
+    if (r != PA_OK || fused) return r;
+  }
+  // Not fusable here (other kernel, odd alignment): the scatter, then decode.
+  const int64_t s1 = head_dim, s0 = (int64_t)num_kv_heads * head_dim;
+  const int r = pa_kv_scatter(new_k, s0, s1, 1, new_v, s0, s1, 1, dtype, slot_mapping, 1, batch, k_pool_layer,
+                              v_pool_layer, num_blocks * (int64_t)block_size, num_kv_heads, head_dim, dtype, stream);
+  if (r != PA_OK) return r;
+  return pa_paged_decode(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads, head_dim,
+                         block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch, num_q_heads, scale,
+                         dtype, 0, workspace, workspace_bytes, stream);
+}
+
+namespace pa {
+namespace {
+
+int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_layer, const void* v_pool_layer,
+                int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
+                int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
+                int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
+                void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused) {
   if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0 ||
       block_size <= 0 || num_blocks <= 0 || bt_width <= 0 || partition_tokens < 0)
     return PA_ERR_INVALID;
@@ -1001,6 +1096,13 @@ extern "C" int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const 
       p.part_o = reinterpret_cast<float*>(ws + off_ml + ml_bytes);
       p.prefix = reinterpret_cast<int*>(ws + off_ml + ml_bytes + po_bytes);
       p.status = status;
+      p.new_k = fw ? fw->new_k : nullptr;
+      p.new_v = fw ? fw->new_v : nullptr;
+      p.slots = fw ? fw->slots : nullptr;
+      p.k_pool = const_cast<void*>(k_pool_layer);
+      p.v_pool = const_cast<void*>(v_pool_layer);
+      p.num_slots = static_cast<int64_t>(num_blocks) * block_size;
+      if (fused != nullptr) *fused = fw != nullptr;
       constexpr int CT = kFlatCtasPerSm;
       if (dtype == PA_DTYPE_BF16)
         return head_dim == 64 ? launch_flat<__nv_bfloat16, 64, kFlatNW64, kFlatST64, CT>(p, tk, tv, pl.grid, st)
@@ -1072,3 +1174,6 @@ extern "C" int pa_paged_decode(const void* q, int64_t q_s0, int64_t q_s1, const 
   g.status = status;
   return launch_attn_generic(g, dtype, pl.splits, st);
 }
+
+}  // namespace
+}  // namespace pa

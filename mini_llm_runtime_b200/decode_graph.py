@@ -32,7 +32,7 @@ import torch
 
 from . import _lib
 from .paged_kv_cache import PagedKVCache
-from .qwen2_attention import check_decode_metadata
+from .qwen2_attention import check_decode_metadata, new_token_blocks_private
 
 
 class PagedDecodeGraph:
@@ -49,6 +49,7 @@ class PagedDecodeGraph:
         partition_tokens: int = 0,
         scale: float | None = None,
         write_kv: bool = True,
+        fuse_write: bool = True,
     ):
         dev = _lib.require_cuda(cache.k_cache, what="PagedDecodeGraph")
         if cache.dtype not in (torch.float16, torch.bfloat16, torch.float32):
@@ -63,6 +64,9 @@ class PagedDecodeGraph:
         self.layers = list(range(cache.num_layers) if layers is None else layers)
         self.host_io = host_io
         self.write_kv = write_kv
+        # The KV write rides in the decode kernel (pa_paged_decode_write)
+        # unless the split-KV path is asked for.
+        self.fuse_write = fuse_write and partition_tokens == 0
         self.scale = (1.0 / math.sqrt(cache.head_dim)) if scale is None else float(scale)
         L, B, H, D, HKV = len(self.layers), batch, num_q_heads, cache.head_dim, cache.num_kv_heads
         dt = cache.dtype
@@ -112,14 +116,14 @@ class PagedDecodeGraph:
         main = torch.cuda.current_stream(self.device)
         L, CH = len(self.layers), self.COPY_CHUNK_LAYERS
         chunks = [(a, min(a + CH, L)) for a in range(0, L, CH)]
+        last_of_chunk = {b - 1: a for a, b in chunks}
         ready = {}
         if io:
             for k in ("slot_mapping", "block_tables", "context_lens"):
                 self._dev_inputs[k].copy_(self.host_inputs[k], non_blocking=True)
             self._h2d.wait_stream(main)
             for ci, (a, b) in enumerate(chunks):
-                ctx = torch.cuda.stream(main if ci == 0 else self._h2d)
-                with ctx:
+                with torch.cuda.stream(main if ci == 0 else self._h2d):
                     for k in ("q", "new_k", "new_v"):
                         self._dev_inputs[k][a:b].copy_(self.host_inputs[k][a:b], non_blocking=True)
                     if ci > 0:
@@ -133,20 +137,30 @@ class PagedDecodeGraph:
                 main.wait_event(ready[i])
             nk, nv, q, o = self.new_k[i], self.new_v[i], self.q[i], self.out[i]
             kp, vp = c.k_cache[layer], c.v_cache[layer]
-            if self.write_kv and not warm:
-                st = lib.pa_kv_scatter(
-                    nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0), nv.stride(1),
-                    nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(), vp.data_ptr(),
-                    num_slots, HKV, D, self._code, stream)
-                _lib.check(st, "pa_kv_scatter")
-            st = lib.pa_paged_decode(
-                q.data_ptr(), q.stride(0), q.stride(1), kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D,
-                self.block_tables.data_ptr(), self.block_tables.stride(0), self.width, self.context_lens.data_ptr(),
-                o.data_ptr(), o.stride(0), o.stride(1), B, H, self.scale, self._code, self.partition_tokens,
-                self.workspace.data_ptr(), self.workspace.numel(), stream)
-            _lib.check(st, "pa_paged_decode")
-            if io and any(i == b - 1 for _, b in chunks):
-                a = max(a for a, b in chunks if b == i + 1)
+            write = self.write_kv and not warm
+            if write and self.fuse_write:
+                st = lib.pa_paged_decode_write(
+                    q.data_ptr(), q.stride(0), q.stride(1), nk.data_ptr(), nv.data_ptr(), self.slot_mapping.data_ptr(),
+                    kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D, self.block_tables.data_ptr(),
+                    self.block_tables.stride(0), self.width, self.context_lens.data_ptr(), o.data_ptr(), o.stride(0),
+                    o.stride(1), B, H, self.scale, self._code, self.workspace.data_ptr(), self.workspace.numel(),
+                    stream)
+                _lib.check(st, "pa_paged_decode_write")
+            else:
+                if write:
+                    st = lib.pa_kv_scatter(
+                        nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0),
+                        nv.stride(1), nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(),
+                        vp.data_ptr(), num_slots, HKV, D, self._code, stream)
+                    _lib.check(st, "pa_kv_scatter")
+                st = lib.pa_paged_decode(
+                    q.data_ptr(), q.stride(0), q.stride(1), kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D,
+                    self.block_tables.data_ptr(), self.block_tables.stride(0), self.width, self.context_lens.data_ptr(),
+                    o.data_ptr(), o.stride(0), o.stride(1), B, H, self.scale, self._code, self.partition_tokens,
+                    self.workspace.data_ptr(), self.workspace.numel(), stream)
+                _lib.check(st, "pa_paged_decode")
+            if io and i in last_of_chunk:
+                a = last_of_chunk[i]
                 done = torch.cuda.Event()
                 done.record(main)
                 self._d2h.wait_event(done)
@@ -172,8 +186,12 @@ class PagedDecodeGraph:
     # -- host-side metadata checks (model/qwen2.py:580-602, paged_kv_cache.py:228-239)
     def validate(self, inputs: dict | None = None) -> None:
         src = self.host_inputs if inputs is None else inputs
-        check_decode_metadata(src["context_lens"].numpy(), src["block_tables"].numpy(), src["slot_mapping"].numpy(),
-                              None, self.cache.block_size, self.cache.num_blocks)
+        lens, tables = src["context_lens"].numpy(), src["block_tables"].numpy()
+        check_decode_metadata(lens, tables, src["slot_mapping"].numpy(), None, self.cache.block_size,
+                              self.cache.num_blocks)
+        if self.write_kv and self.fuse_write and not new_token_blocks_private(lens, tables, self.cache.block_size):
+            raise ValueError("fused KV write needs each new token's block private to its sequence "
+                             "(build the graph with fuse_write=False for shared blocks)")
 
     def run(self, validate: bool = True) -> None:
         """Validate the staged metadata on the host and replay the step on the
@@ -192,5 +210,13 @@ class PagedDecodeGraph:
 
     @property
     def launches_per_step(self) -> int:
-        """Kernels of this library launched per replay."""
-        return (2 if self.write_kv else 1) * len(self.layers)
+        """Kernels of this library launched per replay: per layer the decode
+        (main + combine kernel on the balanced path, one kernel otherwise)
+        and, when the write is not fused into it, the KV scatter."""
+        c = self.cache
+        balanced = (c.dtype in (torch.bfloat16, torch.float16) and c.head_dim in (64, 128) and c.block_size % 16 == 0
+                    and c.block_size <= 256 and self.partition_tokens == 0 and self.batch <= 1024)
+        per_layer = 2 if balanced else 1
+        if self.write_kv and not (self.fuse_write and balanced):
+            per_layer += 1
+        return per_layer * len(self.layers)

@@ -25,6 +25,7 @@ import torch
 from . import _lib
 
 __all__ = [
+    "paged_decode_with_kv_write",
     "paged_attention_decode",
     "paged_attention_decode_batch_parallel",
     "paged_attention_decode_split_kv",
@@ -92,6 +93,76 @@ def _decode_launch(
             int(partition_tokens), ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
         )
     _lib.check(st, "pa_paged_decode")
+    return out
+
+
+def paged_decode_with_kv_write(
+    q: torch.Tensor,
+    new_k: torch.Tensor,
+    new_v: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    block_size: int,
+    scale: float | None = None,
+) -> torch.Tensor:
+    """The decode step of Qwen2Attention.forward_decode_batch_with_cache
+    (model/qwen2.py:608-621) in one fused launch: write the new token's K/V
+    [B, Hkv, D] to ``slot_mapping`` of the layer pools, then decode
+    q [B, Hq, D] over ``seq_lens`` tokens (which include the new one).
+
+    Same results, bit for bit, as ``PagedKVCache.write_slots`` followed by
+    ``paged_attention_decode_batch_parallel``.  ``slot_mapping[b]`` must be
+    the slot of position ``seq_lens[b] - 1`` in ``block_tables[b]`` (what
+    the reference's decode checks enforce) and no other sequence may read it;
+    the caller validates, as ``Qwen2Attention`` and ``PagedDecodeGraph`` do.
+    """
+    if q.ndim != 3 or new_k.ndim != 3 or new_k.shape != new_v.shape:
+        raise ValueError("q must be [B, Hq, D] and new_k / new_v [B, Hkv, D]")
+    _check_caches(k_cache, v_cache)
+    b, hq, d = q.shape
+    nb, bs, hkv, dk = k_cache.shape
+    if tuple(new_k.shape) != (b, hkv, dk) or d != dk:
+        raise ValueError("new_k / new_v must have shape [B, Hkv, D] matching the cache")
+    if hq % hkv != 0:
+        raise ValueError("num_query_heads must be divisible by num_kv_heads")
+    if block_size != bs:
+        raise ValueError("block_size does not match KV cache layout")
+    if slot_mapping.shape != (b,) or block_tables.ndim != 2 or block_tables.shape[0] != b or seq_lens.shape != (b,):
+        raise ValueError("slot_mapping / seq_lens must be [B] and block_tables [B, max_num_blocks]")
+    dev = _lib.require_cuda(q, new_k, new_v, slot_mapping, k_cache, v_cache, block_tables, seq_lens,
+                            what="paged_decode_with_kv_write")
+    _pool_ok(k_cache, v_cache, q.dtype)
+    if new_k.dtype != q.dtype or new_v.dtype != q.dtype:
+        raise TypeError("new_k / new_v must have the KV cache dtype")
+    lib = _lib.load()
+    new_k, new_v = new_k.contiguous(), new_v.contiguous()
+    slots = _as_long(slot_mapping, dev).contiguous()
+    block_tables = _as_long(block_tables, dev)
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    seq_lens = _as_long(seq_lens, dev).contiguous()
+    if q.stride(2) != 1:
+        q = q.contiguous()
+    out = torch.empty((b, hq, d), dtype=q.dtype, device=dev)
+    code = _lib.dtype_code(q.dtype)
+    width = block_tables.shape[1]
+    ws_bytes = lib.pa_decode_workspace_bytes(b, hkv, hq, d, bs, width, 0, code)
+    if ws_bytes == 0:
+        raise ValueError("invalid decode arguments")
+    ws = _lib.decode_workspace(dev, ws_bytes, b, hq)
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    with torch.cuda.device(dev):
+        st = lib.pa_paged_decode_write(
+            q.data_ptr(), q.stride(0), q.stride(1), new_k.data_ptr(), new_v.data_ptr(), slots.data_ptr(),
+            k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d, block_tables.data_ptr(), block_tables.stride(0),
+            width, seq_lens.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), b, hq, float(scale), code,
+            ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
+        )
+    _lib.check(st, "pa_paged_decode_write")
     return out
 
 

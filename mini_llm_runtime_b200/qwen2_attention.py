@@ -37,8 +37,25 @@ from .paged_attention import (
     paged_attention_decode_batch_parallel,
     paged_attention_prefill_chunk_tiled,
     paged_attention_prefill_varlen,
+    paged_decode_with_kv_write,
 )
 from .paged_kv_cache import PagedKVCache
+
+
+def new_token_blocks_private(context_lens: np.ndarray, block_tables: np.ndarray, block_size: int) -> bool:
+    """True when no sequence's context reaches the block that receives
+    another sequence's new token.  The fused write + decode patches the new
+    rows into the decoding sequence's own staged K/V only, so a block shared
+    with another sequence's context must take the unfused write-then-decode
+    order instead."""
+    need = (context_lens + block_size - 1) // block_size
+    width = block_tables.shape[1]
+    used = np.arange(width)[None, :] < need[:, None]
+    pos = context_lens - 1
+    new_blocks = block_tables[np.arange(len(context_lens)), pos // block_size]
+    blocks = block_tables[used]
+    counts = np.bincount(blocks[blocks >= 0], minlength=int(new_blocks.max()) + 1 if len(new_blocks) else 1)
+    return bool(np.all(counts[new_blocks] == 1))
 
 
 def check_decode_metadata(context_lens: np.ndarray, block_tables: np.ndarray, slot_mapping: np.ndarray,
@@ -228,11 +245,16 @@ class Qwen2Attention(nn.Module):
                               host[:batch], kv_cache.block_size, kv_cache.num_blocks)
         k_layer, v_layer = kv_cache.get_layer_cache(layer_idx)
         q, k, v = self.project(hidden_states, position_ids)
-        # Slots were checked above (in range by the table check, distinct).
-        kv_cache.write_slots(slot_mapping=slot_mapping, k=k.squeeze(1), v=v.squeeze(1), layer_idx=layer_idx,
-                             validate=False)
-        out = paged_attention_decode_batch_parallel(q.squeeze(1), k_layer, v_layer, block_tables, context_lens,
-                                                    kv_cache.block_size)
+        lens_h = host[2 * batch:3 * batch]
+        if new_token_blocks_private(lens_h, host[3 * batch:].reshape(batch, w), kv_cache.block_size):
+            # KV write and decode in one launch (slots checked above).
+            out = paged_decode_with_kv_write(q.squeeze(1), k.squeeze(1), v.squeeze(1), slot_mapping, k_layer,
+                                             v_layer, block_tables, context_lens, kv_cache.block_size)
+        else:
+            kv_cache.write_slots(slot_mapping=slot_mapping, k=k.squeeze(1), v=v.squeeze(1), layer_idx=layer_idx,
+                                 validate=False)
+            out = paged_attention_decode_batch_parallel(q.squeeze(1), k_layer, v_layer, block_tables, context_lens,
+                                                        kv_cache.block_size)
         return self.o_proj(out.reshape(batch, 1, self.hidden_size))
 
     # -- model/qwen2.py:624-767 ------------------------------------------------

@@ -251,3 +251,45 @@ def test_decode_graph_step_matches_eager(cuda_device, layers):
     with pytest.raises(ValueError, match="slot_mapping must match"):
         hi["slot_mapping"][0] += 1
         g.run()
+
+
+@pytest.mark.parametrize(
+    "dtype,d,hq,hkv,bs",
+    [
+        (torch.bfloat16, 64, 14, 2, 16),   # config-2 geometry: fused into the balanced kernel
+        (torch.float16, 128, 28, 4, 16),   # config-5 geometry: fused
+        (torch.bfloat16, 64, 8, 1, 32),    # MQA, two boxes per block: fused
+        (torch.bfloat16, 128, 36, 2, 16),  # group of 18: two head tiles, both patch, tile 0 writes
+        (torch.float32, 64, 14, 2, 16),    # FP32: scatter + CUDA-core decode
+        (torch.bfloat16, 64, 14, 2, 8),    # block size 8: scatter + CUDA-core decode
+    ],
+)
+def test_fused_kv_write_matches_scatter_then_decode(cuda_device, dtype, d, hq, hkv, bs):
+    """pa_paged_decode_write == write_slots then decode, bit for bit, for the
+    output and for both pools; the new token lands in every block position
+    (first / middle / last row of a sub-block and of a block)."""
+    from mini_llm_runtime_b200 import paged_decode_with_kv_write
+
+    ctx = [1, 15, 16, 17, 31, 33, 300, 1025, 4096]
+    case = make_decode_case(ctx, hq, hkv, d, bs, dtype, cuda_device, seed=d + hq + bs)
+    g = torch.Generator().manual_seed(99)
+    new_k = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(cuda_device)
+    new_v = torch.randn(len(ctx), hkv, d, generator=g).to(dtype).to(cuda_device)
+    tables, lens = case["tables"], case["lens"]
+    pos = lens - 1
+    slots = tables[torch.arange(len(ctx), device=cuda_device), pos // bs] * bs + pos % bs
+    k1, v1 = case["k"].clone(), case["v"].clone()
+    k2, v2 = case["k"].clone(), case["v"].clone()
+    out = paged_decode_with_kv_write(case["q"], new_k, new_v, slots, k1, v1, tables, lens, bs)
+    k2.view(-1, hkv, d)[slots] = new_k
+    v2.view(-1, hkv, d)[slots] = new_v
+    ref = paged_attention_decode_batch_parallel(case["q"], k2, v2, tables, lens, bs)
+    torch.cuda.synchronize()
+    bits = torch.int32 if dtype == torch.float32 else torch.int16
+    assert torch.equal(out.view(bits), ref.view(bits))
+    assert torch.equal(k1.view(bits), k2.view(bits))
+    assert torch.equal(v1.view(bits), v2.view(bits))
+    # And it is the attention over the written cache (oracle, FP32 math).
+    q_np, _, _, tab_np, ctx_np = case["np"]
+    exp = O.decode_batch(q_np, k2.float().cpu().numpy(), v2.float().cpu().numpy(), tab_np, ctx_np, bs)
+    check(out, exp, dtype)
