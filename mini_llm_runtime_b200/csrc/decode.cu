@@ -545,7 +545,7 @@ constexpr int kCombineThreads = 256;
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatParams p) {
-  __shared__ float smx[16], slt[16];
+  __shared__ float sm_m[kCombineThreads], sm_l[kCombineThreads];
   __shared__ float red[kCombineThreads * 8];
   grid_dep_wait();
   const int seg = blockIdx.x;
@@ -570,63 +570,29 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
     const int sl = (r == 0 && !g0_first) ? 1 : 0;
     return (int64_t)(gg * 2 + sl) * 16;
   };
-  // Phase 1: per row, the max m and the merged l (warp h, lanes over records).
-  for (int h = warp; h < hn; h += kCombineThreads / 32) {
-    float mx = -INFINITY;
-    float2 mine[4];
-    int nm = 0;
-    for (int r = lane; r < nrec; r += 32) {
-      const int64_t base = rec(r);
-      float2 ml = make_float2(-INFINITY, 0.f);
-      if (base >= 0) ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (base + h) * 2));
-      if (nm < 4) mine[nm] = ml;
-      ++nm;
-      mx = fmaxf(mx, ml.x);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float lt = 0.f;
-    int k = 0;
-    for (int r = lane; r < nrec; r += 32, ++k) {
-      float2 ml;
-      if (k < 4) {
-        ml = mine[k];
-      } else {
-        const int64_t base = rec(r);
-        ml = base >= 0 ? __ldcg(reinterpret_cast<const float2*>(p.part_ml + (base + h) * 2))
-                       : make_float2(-INFINITY, 0.f);
-      }
-      if (ml.x != -INFINITY) lt += exp2f(ml.x - mx) * ml.y;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o);
-    if (lane == 0) {
-      smx[h] = mx;
-      slt[h] = lt;
-    }
-  }
-  __syncthreads();
-  // Phase 2: items (row, 8 columns) x stripes of records, reduced in smem.
-  // Records are taken four at a time with every load issued before any is
-  // used, so a stripe of records costs one memory round trip.
+  // One pass: thread (item, stripe) merges the records stripe, stripe +
+  // stripes, ... of one (row, 8 columns) item online (running max in the
+  // log2 domain, rescaled l and O), four records' loads in flight at a
+  // time; then the stripes of each item are merged by log-sum-exp through
+  // shared memory.  One dependent round of global loads per four records.
   const int items = hn * (D / 8);
   const int stripes = kCombineThreads / items;
   const int item = tid % items, stripe = tid / items;
+  float mrun = -INFINITY, lrun = 0.f;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (stripe < stripes) {
     const int h = item / (D / 8), d = 8 * (item - h * (D / 8));
-    const float mx = smx[h];
     for (int r0 = stripe; r0 < nrec; r0 += 4 * stripes) {
-      float m[4];
+      float2 ml[4];
       float4 v0[4], v1[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int r = r0 + u * stripes;
         const int64_t base = r < nrec ? rec(r) : -1;
-        m[u] = -INFINITY;
+        ml[u] = make_float2(-INFINITY, 0.f);
         v0[u] = v1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (base >= 0) {
-          m[u] = __ldcg(p.part_ml + (base + h) * 2);
+          ml[u] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (base + h) * 2));
           const float4* src = reinterpret_cast<const float4*>(p.part_o + (base + h) * D + d);
           v0[u] = __ldcg(src);
           v1[u] = __ldcg(src + 1);
@@ -634,31 +600,43 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
       }
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float wt = m[u] == -INFINITY ? 0.f : exp2f(m[u] - mx);
-        acc[0] = fmaf(wt, v0[u].x, acc[0]);
-        acc[1] = fmaf(wt, v0[u].y, acc[1]);
-        acc[2] = fmaf(wt, v0[u].z, acc[2]);
-        acc[3] = fmaf(wt, v0[u].w, acc[3]);
-        acc[4] = fmaf(wt, v1[u].x, acc[4]);
-        acc[5] = fmaf(wt, v1[u].y, acc[5]);
-        acc[6] = fmaf(wt, v1[u].z, acc[6]);
-        acc[7] = fmaf(wt, v1[u].w, acc[7]);
+        if (ml[u].x == -INFINITY) continue;
+        const float mnew = fmaxf(mrun, ml[u].x);
+        const float a = exp2f(mrun - mnew), wt = exp2f(ml[u].x - mnew);  // a = 0 on the first record
+        lrun = lrun * a + ml[u].y * wt;
+        acc[0] = fmaf(wt, v0[u].x, acc[0] * a);
+        acc[1] = fmaf(wt, v0[u].y, acc[1] * a);
+        acc[2] = fmaf(wt, v0[u].z, acc[2] * a);
+        acc[3] = fmaf(wt, v0[u].w, acc[3] * a);
+        acc[4] = fmaf(wt, v1[u].x, acc[4] * a);
+        acc[5] = fmaf(wt, v1[u].y, acc[5] * a);
+        acc[6] = fmaf(wt, v1[u].z, acc[6] * a);
+        acc[7] = fmaf(wt, v1[u].w, acc[7] * a);
+        mrun = mnew;
       }
     }
   }
+  sm_m[tid] = mrun;
+  sm_l[tid] = lrun;
 #pragma unroll
   for (int e = 0; e < 8; ++e) red[tid * 8 + e] = acc[e];
   __syncthreads();
   if (tid < items) {
     const int h = tid / (D / 8), d = 8 * (tid - h * (D / 8));
-    float sum[8];
+    float mx = -INFINITY;
+    for (int s2 = 0; s2 < stripes; ++s2) mx = fmaxf(mx, sm_m[s2 * items + tid]);
+    float lt = 0.f, sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s2 = 0; s2 < stripes; ++s2) {
+      const int t2 = s2 * items + tid;
+      const float ms = sm_m[t2];
+      if (ms == -INFINITY) continue;
+      const float wt = exp2f(ms - mx);
+      lt = fmaf(sm_l[t2], wt, lt);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sum[e] = red[tid * 8 + e];
-    for (int s2 = 1; s2 < stripes; ++s2)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) sum[e] += red[(s2 * items + tid) * 8 + e];
+      for (int e = 0; e < 8; ++e) sum[e] = fmaf(red[t2 * 8 + e], wt, sum[e]);
+    }
     T* out = reinterpret_cast<T*>(p.out);
-    store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d, sum, 1.f / slt[h]);
+    store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d, sum, 1.f / lt);
   }
 }
 
