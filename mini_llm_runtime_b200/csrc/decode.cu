@@ -547,11 +547,45 @@ template <typename T, int D>
 __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatParams p) {
   __shared__ float sm_m[kCombineThreads], sm_l[kCombineThreads];
   __shared__ float red[kCombineThreads * 8];
-  grid_dep_wait();
+  __shared__ int wsum[2][kCombineThreads / 32];
   const int seg = blockIdx.x;
   const int b = seg / p.SPS, segx = seg - b * p.SPS;
-  const int pb0 = p.prefix[b], pb1 = p.prefix[b + 1], ptot = p.prefix[p.B];
-  const int nsub = pb1 - pb0;
+  // The slice boundaries follow from the context lengths alone, an input
+  // the main kernel does not write: recompute this sequence's sub-block
+  // offset and the batch total before waiting for the main kernel (PDL), so
+  // only the record loads remain after the wait.
+  int pb0, nsub, ptot;
+  {
+    const int64_t cap = p.bt_width * (int64_t)p.bs;
+    int before = 0, all = 0;
+    for (int i = threadIdx.x; i < p.B; i += kCombineThreads) {
+      int64_t ctx = p.context_lens[i];
+      ctx = ctx > cap ? cap : ctx;
+      const int c = ctx > 0 ? static_cast<int>((ctx + kSub - 1) / kSub) : 0;
+      all += c;
+      before += i < b ? c : 0;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, o);
+      all += __shfl_xor_sync(0xffffffffu, all, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+      wsum[0][threadIdx.x >> 5] = before;
+      wsum[1][threadIdx.x >> 5] = all;
+    }
+    __syncthreads();
+    pb0 = 0;
+    ptot = 0;
+#pragma unroll
+    for (int w = 0; w < kCombineThreads / 32; ++w) {
+      pb0 += wsum[0][w];
+      ptot += wsum[1][w];
+    }
+    int64_t ctx = p.context_lens[b];
+    ctx = ctx > cap ? cap : ctx;
+    nsub = ctx > 0 ? static_cast<int>((ctx + kSub - 1) / kSub) : 0;
+  }
   if (nsub <= 0) return;
   const int W = p.W;
   const int64_t total = (int64_t)ptot * p.SPS;
@@ -560,6 +594,7 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
   const int g1 = static_cast<int>((send * W - 1) / total);
   if (g0 == g1) return;  // finished inside one slice
   const int nrec = g1 - g0 + 1;
+  grid_dep_wait();  // the main kernel's records are complete and visible
   const int kvh = segx / p.HT, ht = segx - kvh * p.HT;
   const int h0 = kvh * p.group + ht * 16, hn = min(16, p.group - ht * 16);
   const bool g0_first = (int64_t)g0 * total / W == sstart;
