@@ -542,9 +542,13 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
 // slice return at once.  Launched with PDL right behind the main kernel; the
 // loads of one stage are issued together so a merge costs a few round trips.
 constexpr int kCombineThreads = 256;
+// At most 64 registers (4 CTAs' worth per SM): a combine CTA then fits beside
+// the two main-kernel CTAs of an SM (2 x 128 threads x 188 registers), so the
+// PDL launch makes it resident early and only the record loads remain after
+// the main kernel ends.
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatParams p) {
+__global__ void __launch_bounds__(kCombineThreads, 4) decode_combine_kernel(FlatParams p) {
   __shared__ float sm_m[kCombineThreads], sm_l[kCombineThreads];
   __shared__ float red[kCombineThreads * 8];
   __shared__ int wsum[2][kCombineThreads / 32];
