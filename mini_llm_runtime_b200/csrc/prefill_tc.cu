@@ -57,7 +57,7 @@ namespace {
 
 constexpr int kM = 128;                      // MMA rows per M-tile
 constexpr int kThreads = 384;                // 3 warpgroups
-constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kProducerWarp = 8, kMmaWarp = 9, kSchedWarp = 10;
 constexpr int kConsumerWarps = 9;            // MMA warp + 8 softmax warps read each item index
 // setmaxnreg budgets (per thread): launch gives 168 x 384; the control
 // warpgroup drops to 64 so the two softmax warpgroups can hold a 128-float
@@ -65,8 +65,15 @@ constexpr int kConsumerWarps = 9;            // MMA warp + 8 softmax warps read 
 constexpr int kCtrlRegs = 64, kSoftmaxRegs = 216;
 constexpr float kRescaleLog2 = 8.f;          // lazy-rescale threshold (log2 units)
 constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
-#ifndef PA_PREFILL_POLY_PAIRS
-#define PA_PREFILL_POLY_PAIRS 0                  // of every 8 column pairs, exp2 on the FMA pipe
+// Of every 8 column pairs of a score row, how many take the FMA-pipe exp2
+// (the rest the MUFU one).  head_dim 64 is bound by the exponentials and
+// gains from moving a quarter of them; head_dim 128 has twice the tensor
+// work per score and is not.
+#ifndef PA_PREFILL_POLY64
+#define PA_PREFILL_POLY64 2
+#endif
+#ifndef PA_PREFILL_POLY128
+#define PA_PREFILL_POLY128 0
 #endif
 
 template <int D> struct Shape;
@@ -176,7 +183,6 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // (max relative error 1.0e-4, far below the 2^-9 of the BF16/F16 P it
 // feeds), and 2^n applied by adding n to the exponent field.  Inputs are
 // clamped to >= -127 (-inf -> exactly 0); they never exceed +8 here.
-constexpr int kPolyPairsPer8 = PA_PREFILL_POLY_PAIRS;
 __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   constexpr float kShift = 12582912.f;  // 1.5 * 2^23
   x.x = fmaxf(x.x, -127.f);
@@ -192,6 +198,21 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 }
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b) { return MmaOp<T>::pack(a, b); }
+
+// Rendezvous of the MMA warp and the scheduler warp on named barrier 1 (64
+// threads, no shared-memory access); returns how many of the 64 threads
+// voted to abort.
+__device__ __forceinline__ int rendezvous(bool abort) {
+  int n;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.popc.u32 %0, 1, 64, p;\n\t}"
+      : "=r"(n)
+      : "r"(abort ? 1u : 0u)
+      : "memory");
+  return n;
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -218,6 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   volatile int* ring = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 16);
+  volatile int* sched_box = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);  // item index, tiles
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -364,88 +386,156 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-      constexpr uint32_t idesc_s = tc::instr_desc_f16(kBf16, kM, N, false, false);
-      constexpr uint32_t idesc_o = tc::instr_desc_f16(kBf16, kM, D, false, true);
-      const uint32_t sbase = smem_u32(smem);
-      // Descriptor words of the first buffer of each operand (SW128, SBO
-      // 1024; V is MN-major with its 64-column halves N*128 bytes apart).
-      constexpr uint32_t kHi = tc::desc_hi_sw128(1024);
-      const uint32_t q_lo = tc::desc_lo(sbase + L::kOffQ, 16);
-      const uint32_t k_lo = tc::desc_lo(sbase + L::kOffK, 16);
-      const uint32_t v_lo = tc::desc_lo(sbase + L::kOffV, N * 128);
-      uint32_t li = 0, g = 0;
-      bool ok = true;
-      // O_w += P_w V(stage) for the tile whose softmax was the t-th of group w.
-      auto issue_pv = [&](int w, uint32_t t, int stage, bool accumulate, bool first_of_item) {
-        if (ok) ok = mbar_wait(&p_full[w], t & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-        if (ok && first_of_item && li > 0) ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-        if (!ok) return;
-        tc::fence_after_sync();
-        // P_w is read from TMEM (8 columns per K=16 step), V from shared
-        // memory; one add per MMA (compile-time offsets).
-        const uint32_t a0 = tmem + w * L::kWgCols + L::kTmemP;
-        const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
-        const uint32_t d = tmem + w * L::kWgCols + L::kTmemO;
-        tc::mma_ts_words(d, a0, b0, kHi, idesc_o, accumulate ? 1u : 0u);
+    // This warp never waits on an mbarrier (such a wait stalls the issuing
+    // thread until its MMAs in flight drain, idling the tensor core): the
+    // scheduler warp does the waiting and releases each step through a
+    // rendezvous on named barrier 1, which also carries an abort vote.
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    constexpr uint32_t idesc_s = tc::instr_desc_f16(kBf16, kM, N, false, false);
+    constexpr uint32_t idesc_o = tc::instr_desc_f16(kBf16, kM, D, false, true);
+    const uint32_t sbase = smem_u32(smem);
+    // Descriptor words of the first buffer of each operand (SW128, SBO
+    // 1024; V is MN-major with its 64-column halves N*128 bytes apart).
+    constexpr uint32_t kHi = tc::desc_hi_sw128(1024);
+    const uint32_t q_lo = tc::desc_lo(sbase + L::kOffQ, 16);
+    const uint32_t k_lo = tc::desc_lo(sbase + L::kOffK, 16);
+    const uint32_t v_lo = tc::desc_lo(sbase + L::kOffV, N * 128);
+    // O_w (+)= P_w V(stage): P_w from TMEM (8 columns per K=16 step), V from
+    // shared memory; one add per MMA (compile-time offsets).
+    auto issue_pv = [&](int w, int stage, bool accumulate) {
+      tc::fence_after_sync();
+      const uint32_t a0 = tmem + w * L::kWgCols + L::kTmemP;
+      const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
+      const uint32_t d = tmem + w * L::kWgCols + L::kTmemO;
+      tc::mma_ts_words(d, a0, b0, kHi, idesc_o, accumulate ? 1u : 0u);
 #pragma unroll
-        for (int kk = 1; kk < N / 16; ++kk)
-          tc::mma_ts_words(d, a0 + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o, 1u);
-        tc::commit(&pv_done[w]);
-      };
-      auto issue_s = [&](int w, int qb, int stage) {
-        const uint32_t a0 = q_lo + (qb * 2 + w) * (L::kQTile >> 4);
-        const uint32_t b0 = k_lo + stage * (L::kKVTile >> 4);
-        const uint32_t d = tmem + w * L::kWgCols + L::kTmemS;
+      for (int kk = 1; kk < N / 16; ++kk)
+        tc::mma_ts_words(d, a0 + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o, 1u);
+      tc::commit(&pv_done[w]);
+    };
+    auto issue_s = [&](int w, int qb, int stage) {
+      tc::fence_after_sync();
+      const uint32_t a0 = q_lo + (qb * 2 + w) * (L::kQTile >> 4);
+      const uint32_t b0 = k_lo + stage * (L::kKVTile >> 4);
+      const uint32_t d = tmem + w * L::kWgCols + L::kTmemS;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          tc::mma_ss_words(d, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4),
-                           b0 + (((kk >> 2) * N * 128 + (kk & 3) * 32) >> 4), kHi, idesc_s, kk > 0 ? 1u : 0u);
-        tc::commit(&s_full[w]);
-      };
-      for (uint32_t cons = 0; ok; ++cons) {
-        const int rs = cons % L::kRing;
-        ok = mbar_wait(&item_full[rs], (cons / L::kRing) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-        const int idx = ring[rs];
-        mbar_arrive(&item_empty[rs]);
-        if (!ok || idx < 0) break;
-        Item it;
-        item_at(p, idx, N, it);
-        const int qb = li % QB;
-        ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-        for (int j = 0; j < it.ntiles && ok; ++j, ++g) {
-          const int st = g % ST;
-          ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-          if (ok && *abort_flag) ok = false;
-          if (!ok) break;
-          tc::fence_after_sync();
-          // S_w(g) as soon as the softmax has read S_w(g-1) into registers,
-          // then the P V of the previous tile once its P is in TMEM.
-          for (int w = 0; w < 2 && ok; ++w) {
-            if (g > 0) ok = mbar_wait(&s_free[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-            if (!ok) break;
-            tc::fence_after_sync();
-            issue_s(w, qb, st);
-          }
-          if (ok && j > 0) {
-            for (int w = 0; w < 2 && ok; ++w) issue_pv(w, g - 1, (g - 1) % ST, j > 1, j == 1);
-            if (ok) tc::commit(&kv_empty[(g - 1) % ST]);
-          }
+      for (int kk = 0; kk < D / 16; ++kk)
+        tc::mma_ss_words(d, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4),
+                         b0 + (((kk >> 2) * N * 128 + (kk & 3) * 32) >> 4), kHi, idesc_s, kk > 0 ? 1u : 0u);
+      tc::commit(&s_full[w]);
+    };
+    uint32_t li = 0, g = 0;
+    bool aborted = false;
+    for (;;) {
+      if (rendezvous(false)) { aborted = true; break; }  // item published
+      const int idx = sched_box[0], ntiles = sched_box[1];
+      if (idx < 0) break;
+      const int qb = li % QB;
+      for (int j = 0; j < ntiles && !aborted; ++j, ++g) {
+        const int st = g % ST;
+        // S_w(g) once K(g) is in and the softmax has read S_w(g-1) ...
+        for (int w = 0; w < 2 && !aborted; ++w) {
+          if (rendezvous(false)) { aborted = true; break; }
+          if (lane == 0) issue_s(w, qb, st);
         }
-        if (!ok) break;
-        // Last P V of the item, then release its K/V stage and Q buffer.
-        for (int w = 0; w < 2 && ok; ++w) issue_pv(w, g - 1, (g - 1) % ST, it.ntiles > 1, it.ntiles == 1);
-        if (!ok) break;
+        // ... then the P V of the previous tile once its P is in TMEM.
+        if (j > 0) {
+          for (int w = 0; w < 2 && !aborted; ++w) {
+            if (rendezvous(false)) { aborted = true; break; }
+            if (lane == 0) issue_pv(w, (g - 1) % ST, j > 1);
+          }
+          if (!aborted && lane == 0) tc::commit(&kv_empty[(g - 1) % ST]);
+        }
+      }
+      if (aborted) break;
+      // Last P V of the item, then release its K/V stage and Q buffer.
+      for (int w = 0; w < 2 && !aborted; ++w) {
+        if (rendezvous(false)) { aborted = true; break; }
+        if (lane == 0) issue_pv(w, (g - 1) % ST, ntiles > 1);
+      }
+      if (aborted) break;
+      if (lane == 0) {
         tc::commit(&kv_empty[(g - 1) % ST]);
         tc::commit(&q_empty[qb]);
-        ++li;
       }
-      if (!ok) *abort_flag = 1;
+      ++li;
+    }
+    if (lane == 0) {
+      if (aborted) *abort_flag = 1;
       // Every MMA issued has retired before TMEM is released.
       tc::commit(mma_done);
       mbar_wait(mma_done, 0, p.status, PA_DEVICE_TIMEOUT_MMA);
     }
+    __syncwarp();
+  } else if (warp == kSchedWarp) {
+    // ------------------------------------------------------------ scheduler
+    // Waits on every barrier the MMA issuer depends on, in the issuer's
+    // order, and releases it step by step (the same rendezvous sequence,
+    // so both warps pass named barrier 1 equally often on every path).
+    uint32_t li = 0, g = 0;
+    bool ok = true, aborted = false;
+    auto step = [&](bool wait_ok) {  // lane 0 waited; warp-wide release + vote
+      ok = __shfl_sync(0xffffffffu, ok && wait_ok && !*abort_flag, 0);
+      return rendezvous(!ok) != 0;
+    };
+    for (uint32_t cons = 0;; ++cons) {
+      int idx = -1, ntiles = 0;
+      bool w_ok = true;
+      if (lane == 0) {
+        const int rs = cons % L::kRing;
+        w_ok = ok && mbar_wait(&item_full[rs], (cons / L::kRing) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+        if (w_ok) {
+          idx = ring[rs];
+          mbar_arrive(&item_empty[rs]);
+          Item it;
+          if (idx >= 0 && item_at(p, idx, N, it)) ntiles = it.ntiles;
+          else idx = -1;
+        }
+        sched_box[0] = idx;
+        sched_box[1] = ntiles;
+      }
+      idx = __shfl_sync(0xffffffffu, idx, 0);
+      ntiles = __shfl_sync(0xffffffffu, ntiles, 0);
+      if (step(w_ok)) { aborted = true; break; }
+      if (idx < 0) break;
+      const int qb = li % QB;
+      for (int j = 0; j < ntiles && !aborted; ++j, ++g) {
+        const int st = g % ST;
+        for (int w = 0; w < 2 && !aborted; ++w) {
+          w_ok = true;
+          if (lane == 0) {
+            if (w == 0 && j == 0) w_ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+            if (w_ok && w == 0) w_ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+            if (w_ok && g > 0) w_ok = mbar_wait(&s_free[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+          }
+          if (step(w_ok)) aborted = true;
+        }
+        if (j > 0) {
+          for (int w = 0; w < 2 && !aborted; ++w) {
+            w_ok = true;
+            if (lane == 0) {
+              w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+              if (w_ok && j == 1 && li > 0)
+                w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+            }
+            if (step(w_ok)) aborted = true;
+          }
+        }
+      }
+      if (aborted) break;
+      for (int w = 0; w < 2 && !aborted; ++w) {
+        w_ok = true;
+        if (lane == 0) {
+          w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+          if (w_ok && ntiles == 1 && li > 0)
+            w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+        }
+        if (step(w_ok)) aborted = true;
+      }
+      if (aborted) break;
+      ++li;
+    }
+    if (aborted && lane == 0) *abort_flag = 1;
   }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
@@ -551,8 +641,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           }
         }
         // P = 2^(s * scale_log2 - m_run), two columns per packed FP32 op;
-        // kPolyPairsPer8 of every 8 column pairs use the FMA-pipe exp2, the
+        // kPoly of every 8 column pairs use the FMA-pipe exp2, the
         // rest the MUFU one, so the two pipes share the load.
+        constexpr int kPoly = D == 64 ? PA_PREFILL_POLY64 : PA_PREFILL_POLY128;
         const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
         const float2 negm2 = make_float2(-m_run, -m_run);
         float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
@@ -564,7 +655,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             const int q = c * 4 + h;
             const float2 x = __ffma2_rn(make_float2(SV(2 * q), SV(2 * q + 1)), sc2, negm2);
             float2 e;
-            if ((q & 7) < kPolyPairsPer8) {
+            if ((q & 7) < kPoly) {
               e = exp2_poly2(x);
             } else {
               e.x = fast_exp2(x.x);
