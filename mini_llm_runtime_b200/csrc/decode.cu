@@ -602,7 +602,7 @@ __global__ void __launch_bounds__(kCombineThreads, 4) decode_combine_kernel(Flat
   const int kvh = segx / p.HT, ht = segx - kvh * p.HT;
   const int h0 = kvh * p.group + ht * 16, hn = min(16, p.group - ht * 16);
   const bool g0_first = (int64_t)g0 * total / W == sstart;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   auto rec = [&](int r) -> int64_t {  // record row base (h = 0), or -1 for an empty slice
     const int gg = g0 + r;
     if ((int64_t)gg * total / W == (int64_t)(gg + 1) * total / W) return -1;
