@@ -60,9 +60,10 @@ constexpr int kThreads = 384;                // 3 warpgroups
 constexpr int kProducerWarp = 8, kMmaWarp = 9, kSchedWarp = 10;
 constexpr int kConsumerWarps = 9;            // MMA warp + 8 softmax warps read each item index
 // setmaxnreg budgets (per thread): launch gives 168 x 384; the control
-// warpgroup drops to 64 so the two softmax warpgroups can hold a 128-float
-// S row: 4*32*64 + 8*32*216 <= 384*168.
-constexpr int kCtrlRegs = 64, kSoftmaxRegs = 216;
+// warpgroup drops to 56 so the two softmax warpgroups can hold a 128-float
+// S row next to a 32-column O slice: 4*32*56 + 8*32*224 = 384*168.
+constexpr int kCtrlRegs = 56, kSoftmaxRegs = 224;
+static_assert(4 * 32 * kCtrlRegs + 8 * 32 * kSoftmaxRegs <= kThreads * 168, "register split");
 constexpr float kRescaleLog2 = 8.f;          // lazy-rescale threshold (log2 units)
 constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
 // Of every 8 column pairs of a score row, how many take the FMA-pipe exp2
@@ -76,14 +77,40 @@ constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
 #define PA_PREFILL_POLY128 0
 #endif
 
+// head_dim 128 takes 128-token KV tiles with P written over S's TMEM
+// columns (O 128 + S 128 fill an M-tile's 256); 0 selects 64-token tiles
+// with P in columns of its own.
+#ifndef PA_PREFILL_D128_ALIAS
+#define PA_PREFILL_D128_ALIAS 1
+#endif
+
 template <int D> struct Shape;
-// N = KV tokens per tile, ST = K/V ring stages, QB = Q buffers (items in flight).
-template <> struct Shape<64> { static constexpr int N = 128, ST = 4, QB = 2; };
-template <> struct Shape<128> { static constexpr int N = 64, ST = 3, QB = 2; };
+// N = KV tokens per tile, ST = K/V ring stages, QB = Q buffers (items in
+// flight), kAliasP = P overwrites S in TMEM.
+template <> struct Shape<64> {
+  static constexpr int N = 128, ST = 4, QB = 2;
+  static constexpr bool kAliasP = false;
+};
+#if PA_PREFILL_D128_ALIAS
+template <> struct Shape<128> {
+  static constexpr int N = 128, ST = 2, QB = 1;
+  static constexpr bool kAliasP = true;
+};
+#else
+template <> struct Shape<128> {
+  static constexpr int N = 64, ST = 3, QB = 2;
+  static constexpr bool kAliasP = false;
+};
+#endif
 
 template <int D>
 struct Lay {
   static constexpr int N = Shape<D>::N, ST = Shape<D>::ST, QB = Shape<D>::QB;
+  static constexpr bool kAliasP = Shape<D>::kAliasP;
+  // With P over S, K and V have rings of their own (K(g) is free once the
+  // last S that reads it is done, a tile before V(g)), which doubles how far
+  // ahead of use the loads can start; otherwise one ring holds both.
+  static constexpr bool kSplitKV = kAliasP;
   static constexpr int kDH = D / 64;           // 128-byte column slabs per row
   static constexpr int kSlab = kM * 128;       // one 128-row slab (16 KB)
   static constexpr int kQTile = kDH * kSlab;   // Q tile: [kDH][128 rows][128 B]
@@ -93,22 +120,25 @@ struct Lay {
   static constexpr int kOffV = kOffK + ST * kKVTile;
   static constexpr int kOffBar = kOffV + ST * kKVTile;
   static constexpr int kRing = 4;             // claimed item indices in flight
-  static constexpr int kNumBars = 2 * QB + 2 * ST + 10 + 1 + 2 * kRing;
+  static constexpr int kNumBars = 2 * QB + 4 * ST + 10 + 1 + 2 * kRing;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag, item ring
   static constexpr size_t kSmem = 1024 + kOffMisc + 16 + 4 * kRing;
   // TMEM: 256 columns per M-tile w: S (N FP32 columns), P (N/2 columns of
   // packed 16-bit values) and O, each aligned to its width:
   //   D=64,  N=128: S [0,128)  P [128,192)  O [192,256)
+  //   D=128, N=128: O [0,128)  S [128,256), P over S [128,192)
   //   D=128, N=64:  O [0,128)  S [128,192)  P [192,224)
   static constexpr uint32_t kWgCols = 256;
   static constexpr uint32_t kTmemS = D == 64 ? 0 : 128;
-  static constexpr uint32_t kTmemP = kTmemS + N;
+  static constexpr uint32_t kTmemP = kAliasP ? kTmemS : kTmemS + N;
   static constexpr uint32_t kTmemO = D == 64 ? 192 : 0;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr int kBoxes = (N / kBoxTokens) * kDH;  // per K (and per V) tile
   static_assert(kBoxes <= 32, "one TMA box per producer lane");
-  static_assert(kTmemP + N / 2 <= kWgCols && kTmemO + D <= kWgCols &&
-                (kTmemO + D <= kTmemS || kTmemO >= kTmemP + N / 2), "TMEM layout");
+  static constexpr uint32_t kSPEnd = kAliasP ? kTmemS + N : kTmemP + N / 2;
+  static_assert(kSPEnd <= kWgCols && kTmemO + D <= kWgCols && (kTmemO + D <= kTmemS || kTmemO >= kSPEnd),
+                "TMEM layout");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert(N % 32 == 0 && N <= 128, "S row loads in 32-column pieces");
 };
 
@@ -226,9 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + QB;
-  uint64_t* kv_full = q_empty + QB;
+  uint64_t* kv_full = q_empty + QB;   // [ST], K and V of a tile (K only with split rings)
   uint64_t* kv_empty = kv_full + ST;
-  uint64_t* s_full = kv_empty + ST;   // [2], MMA commit after S_w
+  uint64_t* v_full = kv_empty + ST;   // [ST], split rings: V of a tile
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;    // [2], MMA commit after S_w
   uint64_t* s_free = s_full + 2;      // [2], 128 arrivals: S_w read into registers
   uint64_t* p_full = s_free + 2;      // [2], 128 arrivals: P_w in TMEM (and O_w rescaled)
   uint64_t* pv_done = p_full + 2;     // [2], MMA commit after P_w V
@@ -251,6 +283,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     for (int i = 0; i < ST; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -295,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       prefetch_tensormap(&tmap_v);
     }
     uint32_t li = 0, g = 0;  // Q loads issued (one per item), K/V tiles issued
+    bool k_pending = false;  // split rings: K(g) issued, V(g) not yet
     uint32_t pub = 0;        // item indices published to the ring
     int next_static = blockIdx.x;
     bool ok = true;
@@ -355,23 +390,39 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           if (*abort_flag) ok = false;
           if (ok && g >= (uint32_t)ST)
             ok = mbar_wait(&kv_empty[st], ((g / ST) - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-          if (ok) mbar_arrive_expect_tx(&kv_full[st], 2 * L::kKVTile);
+          if (ok) mbar_arrive_expect_tx(&kv_full[st], (L::kSplitKV ? 1 : 2) * L::kKVTile);
         }
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) break;
+        int y = static_cast<int>(p.num_slots);  // out of range -> zero fill
+        int off = 0;
         if (lane < L::kBoxes) {
           const int grp = lane % (N / kBoxTokens), dh = lane / (N / kBoxTokens);
           const int tok = j * N + grp * kBoxTokens;
-          int y = static_cast<int>(p.num_slots);  // out of range -> zero fill
           if (tok < it.ctx) {
             const int64_t pb = __ldg(bt_row + tok / p.bs);
             if (pb >= 0 && pb < p.num_blocks) y = static_cast<int>(pb) * p.bs + tok % p.bs;
           }
-          const int off = st * L::kKVTile + dh * N * 128 + grp * kBoxTokens * 128;
+          off = st * L::kKVTile + dh * N * 128 + grp * kBoxTokens * 128;
           tma_load_3d(smem + L::kOffK + off, &tmap_k, &kv_full[st], dh * 64, it.kvh, y);
-          tma_load_3d(smem + L::kOffV + off, &tmap_v, &kv_full[st], dh * 64, it.kvh, y);
+          if (!L::kSplitKV) tma_load_3d(smem + L::kOffV + off, &tmap_v, &kv_full[st], dh * 64, it.kvh, y);
         }
         __syncwarp();
+        if constexpr (L::kSplitKV) {
+          k_pending = true;
+          if (lane == 0) {
+            if (*abort_flag) ok = false;
+            if (ok && g >= (uint32_t)ST)
+              ok = mbar_wait(&v_empty[st], ((g / ST) - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+            if (ok) mbar_arrive_expect_tx(&v_full[st], L::kKVTile);
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
+          if (lane < L::kBoxes)
+            tma_load_3d(smem + L::kOffV + off, &tmap_v, &v_full[st], (lane / (N / kBoxTokens)) * 64, it.kvh, y);
+          __syncwarp();
+          k_pending = false;
+        }
       }
       if (!ok) break;
     }
@@ -379,8 +430,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     // Copies still in flight (only after an abort) land before exit: the
     // last phase of every stage / Q buffer that was used.
     if (lane == 0) {
-      for (uint32_t x = (g > (uint32_t)ST ? g - ST : 0); x < g; ++x)
+      const uint32_t gk = g + (k_pending ? 1u : 0u);  // K tiles issued
+      for (uint32_t x = (gk > (uint32_t)ST ? gk - ST : 0); x < gk; ++x)
         mbar_wait(&kv_full[x % ST], (x / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+      if (L::kSplitKV)
+        for (uint32_t x = (g > (uint32_t)ST ? g - ST : 0); x < g; ++x)
+          mbar_wait(&v_full[x % ST], (x / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
       for (uint32_t x = (li > (uint32_t)QB ? li - QB : 0); x < li; ++x)
         mbar_wait(&q_full[x % QB], (x / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
     }
@@ -402,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const uint32_t v_lo = tc::desc_lo(sbase + L::kOffV, N * 128);
     // O_w (+)= P_w V(stage): P_w from TMEM (8 columns per K=16 step), V from
     // shared memory; one add per MMA (compile-time offsets).
-    auto issue_pv = [&](int w, int stage, bool accumulate) {
+    auto issue_pv = [&](int w, int stage, bool accumulate, bool signal) {
       tc::fence_after_sync();
       const uint32_t a0 = tmem + w * L::kWgCols + L::kTmemP;
       const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
@@ -411,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
       for (int kk = 1; kk < N / 16; ++kk)
         tc::mma_ts_words(d, a0 + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o, 1u);
-      tc::commit(&pv_done[w]);
+      if (signal) tc::commit(&pv_done[w]);
     };
     auto issue_s = [&](int w, int qb, int stage) {
       tc::fence_after_sync();
@@ -433,29 +488,47 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const int qb = li % QB;
       for (int j = 0; j < ntiles && !aborted; ++j, ++g) {
         const int st = g % ST;
-        // S_w(g) once K(g) is in and the softmax has read S_w(g-1) ...
-        for (int w = 0; w < 2 && !aborted; ++w) {
-          if (rendezvous(false)) { aborted = true; break; }
-          if (lane == 0) issue_s(w, qb, st);
-        }
-        // ... then the P V of the previous tile once its P is in TMEM.
-        if (j > 0) {
+        if constexpr (L::kAliasP) {
+          // P_w(g-1) sits in S_w's columns: its P V goes first, then S_w(g)
+          // overwrites them (one thread's MMAs run in issue order), and the
+          // commit after S_w(g) also tells the softmax that O_w holds the P V
+          // of tile g-1.
           for (int w = 0; w < 2 && !aborted; ++w) {
             if (rendezvous(false)) { aborted = true; break; }
-            if (lane == 0) issue_pv(w, (g - 1) % ST, j > 1);
+            if (lane == 0) {
+              if (j > 0) {
+                issue_pv(w, (g - 1) % ST, j > 1, false);
+                if (w == 1) tc::commit(L::kSplitKV ? &v_empty[(g - 1) % ST] : &kv_empty[(g - 1) % ST]);
+              }
+              issue_s(w, qb, st);
+              if (L::kSplitKV && w == 1) tc::commit(&kv_empty[st]);  // K(g) read by both S
+            }
           }
-          if (!aborted && lane == 0) tc::commit(&kv_empty[(g - 1) % ST]);
+        } else {
+          // S_w(g) once K(g) is in and the softmax has read S_w(g-1) ...
+          for (int w = 0; w < 2 && !aborted; ++w) {
+            if (rendezvous(false)) { aborted = true; break; }
+            if (lane == 0) issue_s(w, qb, st);
+          }
+          // ... then the P V of the previous tile once its P is in TMEM.
+          if (j > 0) {
+            for (int w = 0; w < 2 && !aborted; ++w) {
+              if (rendezvous(false)) { aborted = true; break; }
+              if (lane == 0) issue_pv(w, (g - 1) % ST, j > 1, true);
+            }
+            if (!aborted && lane == 0) tc::commit(&kv_empty[(g - 1) % ST]);
+          }
         }
       }
       if (aborted) break;
       // Last P V of the item, then release its K/V stage and Q buffer.
       for (int w = 0; w < 2 && !aborted; ++w) {
         if (rendezvous(false)) { aborted = true; break; }
-        if (lane == 0) issue_pv(w, (g - 1) % ST, ntiles > 1);
+        if (lane == 0) issue_pv(w, (g - 1) % ST, ntiles > 1, true);
       }
       if (aborted) break;
       if (lane == 0) {
-        tc::commit(&kv_empty[(g - 1) % ST]);
+        tc::commit(L::kSplitKV ? &v_empty[(g - 1) % ST] : &kv_empty[(g - 1) % ST]);
         tc::commit(&q_empty[qb]);
       }
       ++li;
@@ -501,24 +574,43 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const int qb = li % QB;
       for (int j = 0; j < ntiles && !aborted; ++j, ++g) {
         const int st = g % ST;
-        for (int w = 0; w < 2 && !aborted; ++w) {
-          w_ok = true;
-          if (lane == 0) {
-            if (w == 0 && j == 0) w_ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-            if (w_ok && w == 0) w_ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-            if (w_ok && g > 0) w_ok = mbar_wait(&s_free[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-          }
-          if (step(w_ok)) aborted = true;
-        }
-        if (j > 0) {
+        if constexpr (L::kAliasP) {
+          // [P V(g-1) +] S(g) of group w: K(g) and Q in, P_w(g-1) written
+          // (so S_w(g-1) was read), O_w read out before the item's first P V.
+          // At j = 0 the previous item's last P_w was waited for at its tail.
           for (int w = 0; w < 2 && !aborted; ++w) {
             w_ok = true;
             if (lane == 0) {
-              w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+              if (w == 0 && j == 0) w_ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+              if (w_ok && w == 0) w_ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+              if (L::kSplitKV && w_ok && w == 0 && j > 0)
+                w_ok = mbar_wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+              if (w_ok && j > 0) w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
               if (w_ok && j == 1 && li > 0)
                 w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
             }
             if (step(w_ok)) aborted = true;
+          }
+        } else {
+          for (int w = 0; w < 2 && !aborted; ++w) {
+            w_ok = true;
+            if (lane == 0) {
+              if (w == 0 && j == 0) w_ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+              if (w_ok && w == 0) w_ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+              if (w_ok && g > 0) w_ok = mbar_wait(&s_free[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+            }
+            if (step(w_ok)) aborted = true;
+          }
+          if (j > 0) {
+            for (int w = 0; w < 2 && !aborted; ++w) {
+              w_ok = true;
+              if (lane == 0) {
+                w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+                if (w_ok && j == 1 && li > 0)
+                  w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+              }
+              if (step(w_ok)) aborted = true;
+            }
           }
         }
       }
@@ -526,7 +618,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       for (int w = 0; w < 2 && !aborted; ++w) {
         w_ok = true;
         if (lane == 0) {
-          w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
+          if (L::kSplitKV && w == 0)
+            w_ok = mbar_wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+          if (w_ok) w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
           if (w_ok && ntiles == 1 && li > 0)
             w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
         }
@@ -573,8 +667,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
         for (int c = 0; c < N / 32; ++c) tc::tmem_ld32(wg_addr + L::kTmemS + c * 32, su + c * 32);
         tc::tmem_wait_ld();
-        tc::fence_before_sync();
-        mbar_arrive(&s_free[w]);  // S_w may now be overwritten by the next tile's S
+        if constexpr (!L::kAliasP) {
+          tc::fence_before_sync();
+          mbar_arrive(&s_free[w]);  // S_w may now be overwritten by the next tile's S
+        }
         if (j >= nfull) {
           const int lim = Lr - j * N;  // keep keys k <= lim
 #pragma unroll
@@ -589,7 +685,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         // P_w overwritten; wait for it only where needed, so the exponentials
         // below overlap it.  (Waiting before every P store also keeps this
         // group at most one p_full phase ahead of the MMA warp.)
-        bool pv_waited = t == 0;
+        // (With P over S, the S_w(t) commit waited for above already covers
+        // the P V of tile t-1.)
+        bool pv_waited = t == 0 || L::kAliasP;
         auto wait_pv = [&]() {
           if (pv_waited) return true;
           pv_waited = true;
@@ -630,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           const int tok = j * N + r;
           if (tok >= it.ctx) {
             const int st = t % ST;
-            if (mbar_wait(&kv_full[st], (t / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA)) {
+            if (mbar_wait(L::kSplitKV ? &v_full[st] : &kv_full[st], (t / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA)) {
 #pragma unroll
               for (int dh = 0; dh < L::kDH; ++dh) {
                 uint8_t* vrow = smem + L::kOffV + st * L::kKVTile + dh * N * 128 + r * 128;
@@ -681,8 +779,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         mbar_arrive(&p_full[w]);
       }
       if (!ok) break;
-      // Epilogue: the item's last P V has landed in O_w.
-      ok = mbar_wait(&pv_done[w], (t - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA) && !*abort_flag;
+      // Epilogue: the item's last P V has landed in O_w (pv_done completes
+      // once per tile, or once per item with P over S).
+      const uint32_t pv_phase = L::kAliasP ? li : t - 1;
+      ok = mbar_wait(&pv_done[w], pv_phase & 1, p.status, PA_DEVICE_TIMEOUT_MMA) && !*abort_flag;
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc::fence_after_sync();
