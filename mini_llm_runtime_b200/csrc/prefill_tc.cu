@@ -21,20 +21,23 @@
 //   warp 8      TMA producer: the item's two Q tiles (3-D boxes {64, G, P}
 //               straight from the packed [T, Hq, D] tensor, double-buffered
 //               across items when shared memory allows), then per KV tile
-//               of N tokens 8 K boxes + 8 V boxes {64, 1, 16} addressed
-//               through the block table into a ring of stages (128-byte
-//               swizzle = canonical UMMA layout).  Tokens at or past the
-//               context use an out-of-range coordinate: TMA fills zeros.
-//   warp 9      TMEM owner + single-thread MMA issuer.  Per KV tile j:
-//               S_w(j) = Q_w K(j)^T for both M-tiles, then
-//               O_w += P_w(j-1) V(j-1) for both.
-//               S = Q K^T reads both operands from shared memory; P V reads
-//               P from tensor memory and V from shared memory, which halves
-//               the shared-memory traffic of the tile.  S, P and O of each
-//               M-tile have their own TMEM columns, so S_w(j+1) is issued as
-//               soon as the softmax has copied S_w(j) into registers: the
-//               next tile's scores are ready when the softmax finishes this
-//               one, and the P V runs behind it.
+//               of N tokens the K and V boxes {64, 1, 16} addressed through
+//               the block table into rings of stages (128-byte swizzle =
+//               canonical UMMA layout).  Tokens at or past the context use an
+//               out-of-range coordinate: TMA fills zeros.
+//   warps 9-10  MMA issuers, one per M-tile w (warp 9 also owns TMEM): per
+//               KV tile j, S_w(j) = Q_w K(j)^T (both operands from shared
+//               memory) and O_w += P_w(j-1) V(j-1) (P from tensor memory, V
+//               from shared memory, half the shared-memory traffic of an SS
+//               MMA).  Head dim 64 gives S, P and O columns of their own, so
+//               S_w(j+1) is issued as soon as the softmax has copied S_w(j)
+//               into registers.  Head dim 128 fills an M-tile's 256 columns
+//               with O and a 128-key S, writes P over S, and issues
+//               P_w(j-1) V(j-1) before S_w(j) (one thread's MMAs run in
+//               order).  Each issuer does its own mbarrier waits: the
+//               stall such a wait costs right after a thread's MMAs is
+//               covered by the other issuer's MMAs, and one M-tile's chain
+//               never waits for the other's.
 //   warps 0-3   softmax of M-tile 0, warps 4-7 softmax of M-tile 1 (one row
 //               per thread, FP32 statistics in the log2 domain).  While one
 //               group exponentiates, the tensor core works for the other.
@@ -42,7 +45,7 @@
 //               a row's running maximum grows by more than 2^8 (the
 //               unnormalised P then stays below 256, exact enough in FP32 and
 //               BF16), and read once at the end for 1/l and the store.
-//   warps 10-11 idle.
+//   warp 11     idle.
 // Every mbarrier wait is bounded; a failed wait records a status code, sets
 // a CTA-wide abort flag, and every role winds down (in-flight copies and
 // MMAs are drained, TMEM is freed) without further waiting.
@@ -57,8 +60,8 @@ namespace {
 
 constexpr int kM = 128;                      // MMA rows per M-tile
 constexpr int kThreads = 384;                // 3 warpgroups
-constexpr int kProducerWarp = 8, kMmaWarp = 9, kSchedWarp = 10;
-constexpr int kConsumerWarps = 9;            // MMA warp + 8 softmax warps read each item index
+constexpr int kProducerWarp = 8, kMmaWarp0 = 9, kMmaWarp1 = 10;
+constexpr int kConsumerWarps = 10;           // 2 MMA warps + 8 softmax warps read each item index
 // setmaxnreg budgets (per thread): launch gives 168 x 384; the control
 // warpgroup drops to 56 so the two softmax warpgroups can hold a 128-float
 // S row next to a 32-column O slice: 4*32*56 + 8*32*224 = 384*168.
@@ -75,6 +78,20 @@ constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
 #endif
 #ifndef PA_PREFILL_POLY128
 #define PA_PREFILL_POLY128 0
+#endif
+// Waits of the MMA issuers and of the softmax on its scores: 1 polls
+// (test_wait; the waiter is on the critical path and wakes sooner), 0
+// suspends in try_wait (its issue slots stay with the other warps of its
+// SMSP).  Head dim 128 keeps the softmax wait suspended: there the other
+// group's exponentials run beside it.
+#ifndef PA_PREFILL_SPIN_ISSUER
+#define PA_PREFILL_SPIN_ISSUER 1
+#endif
+#ifndef PA_PREFILL_SPIN_SOFTMAX64
+#define PA_PREFILL_SPIN_SOFTMAX64 1
+#endif
+#ifndef PA_PREFILL_SPIN_SOFTMAX128
+#define PA_PREFILL_SPIN_SOFTMAX128 0
 #endif
 
 // head_dim 128 takes 128-token KV tiles with P written over S's TMEM
@@ -120,7 +137,7 @@ struct Lay {
   static constexpr int kOffV = kOffK + ST * kKVTile;
   static constexpr int kOffBar = kOffV + ST * kKVTile;
   static constexpr int kRing = 4;             // claimed item indices in flight
-  static constexpr int kNumBars = 2 * QB + 4 * ST + 10 + 1 + 2 * kRing;
+  static constexpr int kNumBars = 2 * QB + 5 * ST + 10 + 2 + 2 * kRing;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag, item ring
   static constexpr size_t kSmem = 1024 + kOffMisc + 16 + 4 * kRing;
   // TMEM: 256 columns per M-tile w: S (N FP32 columns), P (N/2 columns of
@@ -229,21 +246,6 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b) { return MmaOp<T>::pack(a, b); }
 
-// Rendezvous of the MMA warp and the scheduler warp on named barrier 1 (64
-// threads, no shared-memory access); returns how many of the 64 threads
-// voted to abort.
-__device__ __forceinline__ int rendezvous(bool abort) {
-  int n;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.popc.u32 %0, 1, 64, p;\n\t}"
-      : "=r"(n)
-      : "r"(abort ? 1u : 0u)
-      : "memory");
-  return n;
-}
-
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                                                 const __grid_constant__ CUtensorMap tmap_k,
@@ -265,26 +267,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   uint64_t* p_full = s_free + 2;      // [2], 128 arrivals: P_w in TMEM (and O_w rescaled)
   uint64_t* pv_done = p_full + 2;     // [2], MMA commit after P_w V
   uint64_t* o_empty = pv_done + 2;    // [2], 128 arrivals once an item's O is read out
-  uint64_t* mma_done = o_empty + 2;
-  uint64_t* item_full = mma_done + 1;          // [kRing], producer publishes an index
+  uint64_t* mma_done = o_empty + 2;  // [2], per issuer
+  uint64_t* turn = mma_done + 2;     // [ST], issuer 0 has issued its MMAs of a tile
+  uint64_t* item_full = turn + ST;             // [kRing], producer publishes an index
   uint64_t* item_empty = item_full + L::kRing;  // [kRing], 9 consumer warps took it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   volatile int* ring = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 16);
-  volatile int* sched_box = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 8);  // item index, tiles
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < QB; ++i) {
       mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
+      mbar_init(&q_empty[i], 2);  // a commit from each issuer
     }
     for (int i = 0; i < ST; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], 2);
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
+      mbar_init(&v_empty[i], 2);
+      mbar_init(&turn[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -293,7 +296,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       mbar_init(&pv_done[i], 1);
       mbar_init(&o_empty[i], 128);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(&mma_done[0], 1);
+    mbar_init(&mma_done[1], 1);
     for (int i = 0; i < L::kRing; ++i) {
       mbar_init(&item_full[i], 1);
       mbar_init(&item_empty[i], kConsumerWarps);
@@ -301,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kMmaWarp) {
+  if (warp == kMmaWarp0) {
     tc::tmem_alloc(tmem_slot, L::kTmemCols);
     tc::tmem_relinquish();
   }
@@ -439,197 +443,131 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       for (uint32_t x = (li > (uint32_t)QB ? li - QB : 0); x < li; ++x)
         mbar_wait(&q_full[x % QB], (x / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
     }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    // This warp never waits on an mbarrier (such a wait stalls the issuing
-    // thread until its MMAs in flight drain, idling the tensor core): the
-    // scheduler warp does the waiting and releases each step through a
-    // rendezvous on named barrier 1, which also carries an abort vote.
-    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-    constexpr uint32_t idesc_s = tc::instr_desc_f16(kBf16, kM, N, false, false);
-    constexpr uint32_t idesc_o = tc::instr_desc_f16(kBf16, kM, D, false, true);
-    const uint32_t sbase = smem_u32(smem);
-    // Descriptor words of the first buffer of each operand (SW128, SBO
-    // 1024; V is MN-major with its 64-column halves N*128 bytes apart).
-    constexpr uint32_t kHi = tc::desc_hi_sw128(1024);
-    const uint32_t q_lo = tc::desc_lo(sbase + L::kOffQ, 16);
-    const uint32_t k_lo = tc::desc_lo(sbase + L::kOffK, 16);
-    const uint32_t v_lo = tc::desc_lo(sbase + L::kOffV, N * 128);
-    // O_w (+)= P_w V(stage): P_w from TMEM (8 columns per K=16 step), V from
-    // shared memory; one add per MMA (compile-time offsets).
-    auto issue_pv = [&](int w, int stage, bool accumulate, bool signal) {
-      tc::fence_after_sync();
-      const uint32_t a0 = tmem + w * L::kWgCols + L::kTmemP;
-      const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
-      const uint32_t d = tmem + w * L::kWgCols + L::kTmemO;
-      tc::mma_ts_words(d, a0, b0, kHi, idesc_o, accumulate ? 1u : 0u);
+  } else if (warp == kMmaWarp0 || warp == kMmaWarp1) {
+    // ------------------------------------------------------------ MMA issuers
+    // Warp 9 issues every MMA of M-tile 0, warp 10 every MMA of M-tile 1,
+    // each from its lane 0 and each doing its own waits.  A wait (or any
+    // synchronisation) right after a thread's MMAs stalls that thread for
+    // some hundred cycles; with one issuer per M-tile the other issuer's
+    // MMAs keep the tensor core busy meanwhile, and one M-tile's chain
+    // (softmax -> P V, S -> softmax) never waits for the other's.  Shared
+    // stages (Q, K, V) are released by a commit from each issuer.
+    const int w = warp - kMmaWarp0;
+    if (lane == 0) {
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      constexpr uint32_t idesc_s = tc::instr_desc_f16(kBf16, kM, N, false, false);
+      constexpr uint32_t idesc_o = tc::instr_desc_f16(kBf16, kM, D, false, true);
+      const uint32_t sbase = smem_u32(smem);
+      // Descriptor words of the first buffer of each operand (SW128, SBO
+      // 1024; V is MN-major with its 64-column halves N*128 bytes apart).
+      constexpr uint32_t kHi = tc::desc_hi_sw128(1024);
+      const uint32_t q_lo = tc::desc_lo(sbase + L::kOffQ, 16);
+      const uint32_t k_lo = tc::desc_lo(sbase + L::kOffK, 16);
+      const uint32_t v_lo = tc::desc_lo(sbase + L::kOffV, N * 128);
+      const uint32_t s_tmem = tmem + w * L::kWgCols + L::kTmemS;
+      const uint32_t p_tmem = tmem + w * L::kWgCols + L::kTmemP;
+      const uint32_t o_tmem = tmem + w * L::kWgCols + L::kTmemO;
+      // O_w (+)= P_w V(stage): P_w from TMEM (8 columns per K=16 step), V
+      // from shared memory; one add per MMA (compile-time offsets).
+      auto issue_pv = [&](int stage, bool accumulate, bool signal) {
+        tc::fence_after_sync();
+        const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
+        tc::mma_ts_words(o_tmem, p_tmem, b0, kHi, idesc_o, accumulate ? 1u : 0u);
 #pragma unroll
-      for (int kk = 1; kk < N / 16; ++kk)
-        tc::mma_ts_words(d, a0 + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o, 1u);
-      if (signal) tc::commit(&pv_done[w]);
-    };
-    auto issue_s = [&](int w, int qb, int stage) {
-      tc::fence_after_sync();
-      const uint32_t a0 = q_lo + (qb * 2 + w) * (L::kQTile >> 4);
-      const uint32_t b0 = k_lo + stage * (L::kKVTile >> 4);
-      const uint32_t d = tmem + w * L::kWgCols + L::kTmemS;
+        for (int kk = 1; kk < N / 16; ++kk)
+          tc::mma_ts_words(o_tmem, p_tmem + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o, 1u);
+        if (signal) tc::commit(&pv_done[w]);
+      };
+      // S_w = Q_w K(stage)^T, both from shared memory.
+      auto issue_s = [&](int qb, int stage) {
+        tc::fence_after_sync();
+        const uint32_t a0 = q_lo + (qb * 2 + w) * (L::kQTile >> 4);
+        const uint32_t b0 = k_lo + stage * (L::kKVTile >> 4);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        tc::mma_ss_words(d, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4),
-                         b0 + (((kk >> 2) * N * 128 + (kk & 3) * 32) >> 4), kHi, idesc_s, kk > 0 ? 1u : 0u);
-      tc::commit(&s_full[w]);
-    };
-    uint32_t li = 0, g = 0;
-    bool aborted = false;
-    for (;;) {
-      if (rendezvous(false)) { aborted = true; break; }  // item published
-      const int idx = sched_box[0], ntiles = sched_box[1];
-      if (idx < 0) break;
-      const int qb = li % QB;
-      for (int j = 0; j < ntiles && !aborted; ++j, ++g) {
-        const int st = g % ST;
-        if constexpr (L::kAliasP) {
-          // P_w(g-1) sits in S_w's columns: its P V goes first, then S_w(g)
-          // overwrites them (one thread's MMAs run in issue order), and the
-          // commit after S_w(g) also tells the softmax that O_w holds the P V
-          // of tile g-1.
-          for (int w = 0; w < 2 && !aborted; ++w) {
-            if (rendezvous(false)) { aborted = true; break; }
-            if (lane == 0) {
-              if (j > 0) {
-                issue_pv(w, (g - 1) % ST, j > 1, false);
-                if (w == 1) tc::commit(L::kSplitKV ? &v_empty[(g - 1) % ST] : &kv_empty[(g - 1) % ST]);
-              }
-              issue_s(w, qb, st);
-              if (L::kSplitKV && w == 1) tc::commit(&kv_empty[st]);  // K(g) read by both S
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_ss_words(s_tmem, a0 + (((kk >> 2) * L::kSlab + (kk & 3) * 32) >> 4),
+                           b0 + (((kk >> 2) * N * 128 + (kk & 3) * 32) >> 4), kHi, idesc_s, kk > 0 ? 1u : 0u);
+        tc::commit(&s_full[w]);
+      };
+      bool ok = true;
+      auto wait = [&](uint64_t* bar, uint32_t parity, int code) {
+#if PA_PREFILL_SPIN_ISSUER
+        ok = ok && mbar_wait_spin(bar, parity, p.status, code) && !*abort_flag;
+#else
+        ok = ok && mbar_wait(bar, parity, p.status, code) && !*abort_flag;
+#endif
+        return ok;
+      };
+      uint32_t li = 0, g = 0;
+      for (uint32_t cons = 0; ok; ++cons) {
+        const int rs = cons % L::kRing;
+        if (!wait(&item_full[rs], (cons / L::kRing) & 1, PA_DEVICE_TIMEOUT_TMA)) break;
+        const int idx = ring[rs];
+        mbar_arrive(&item_empty[rs]);
+        Item it;
+        if (idx < 0 || !item_at(p, idx, N, it)) break;
+        const int ntiles = it.ntiles;
+        const int qb = li % QB;
+        for (int j = 0; j < ntiles && ok; ++j, ++g) {
+          const int st = g % ST;
+          if (j == 0) wait(&q_full[qb], (li / QB) & 1, PA_DEVICE_TIMEOUT_TMA);
+          wait(&kv_full[st], (g / ST) & 1, PA_DEVICE_TIMEOUT_TMA);
+          // Issuer 1 queues its MMAs of tile g behind issuer 0's, so the
+          // tensor core finishes M-tile 0's work first and the two softmax
+          // groups stay an MMA group apart instead of exponentiating at the
+          // same time.  (turn[st] completes once per use of stage st; issuer
+          // 0 cannot reuse the stage before issuer 1 has released it.)
+          if (w == 1) wait(&turn[st], (g / ST) & 1, PA_DEVICE_TIMEOUT_MMA);
+          if constexpr (L::kAliasP) {
+            // P_w(g-1) sits in S_w's columns: its P V goes first, then
+            // S_w(g) overwrites them (one thread's MMAs run in issue order),
+            // and the commit after S_w(g) also tells the softmax that O_w
+            // holds the P V of tile g-1.
+            if (j > 0) {
+              wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, PA_DEVICE_TIMEOUT_TMA);
+              wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+              if (j == 1 && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+              if (!ok) break;
+              issue_pv((g - 1) % ST, j > 1, false);
+              tc::commit(&v_empty[(g - 1) % ST]);
             }
-          }
-        } else {
-          // S_w(g) once K(g) is in and the softmax has read S_w(g-1) ...
-          for (int w = 0; w < 2 && !aborted; ++w) {
-            if (rendezvous(false)) { aborted = true; break; }
-            if (lane == 0) issue_s(w, qb, st);
-          }
-          // ... then the P V of the previous tile once its P is in TMEM.
-          if (j > 0) {
-            for (int w = 0; w < 2 && !aborted; ++w) {
-              if (rendezvous(false)) { aborted = true; break; }
-              if (lane == 0) issue_pv(w, (g - 1) % ST, j > 1, true);
+            if (!ok) break;
+            issue_s(qb, st);
+            tc::commit(&kv_empty[st]);  // K(g)
+            if (w == 0) mbar_arrive(&turn[st]);
+          } else {
+            // S_w(g) once K(g) is in and the softmax has read S_w(g-1), then
+            // P_w(g-1) V(g-1) once P_w(g-1) is in TMEM.
+            if (g > 0) wait(&s_free[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+            if (!ok) break;
+            issue_s(qb, st);
+            if (w == 0) mbar_arrive(&turn[st]);
+            if (j > 0) {
+              wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+              if (j == 1 && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+              if (!ok) break;
+              issue_pv((g - 1) % ST, j > 1, true);
+              tc::commit(&kv_empty[(g - 1) % ST]);
             }
-            if (!aborted && lane == 0) tc::commit(&kv_empty[(g - 1) % ST]);
           }
         }
-      }
-      if (aborted) break;
-      // Last P V of the item, then release its K/V stage and Q buffer.
-      for (int w = 0; w < 2 && !aborted; ++w) {
-        if (rendezvous(false)) { aborted = true; break; }
-        if (lane == 0) issue_pv(w, (g - 1) % ST, ntiles > 1, true);
-      }
-      if (aborted) break;
-      if (lane == 0) {
+        if (!ok) break;
+        // Last P V of the item, then release its K/V stage and Q buffer.
+        if (L::kSplitKV) wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, PA_DEVICE_TIMEOUT_TMA);
+        wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+        if (ntiles == 1 && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+        if (!ok) break;
+        issue_pv((g - 1) % ST, ntiles > 1, true);
         tc::commit(L::kSplitKV ? &v_empty[(g - 1) % ST] : &kv_empty[(g - 1) % ST]);
         tc::commit(&q_empty[qb]);
+        ++li;
       }
-      ++li;
-    }
-    if (lane == 0) {
-      if (aborted) *abort_flag = 1;
-      // Every MMA issued has retired before TMEM is released.
-      tc::commit(mma_done);
-      mbar_wait(mma_done, 0, p.status, PA_DEVICE_TIMEOUT_MMA);
+      if (!ok) *abort_flag = 1;
+      // Every MMA this thread issued has retired before TMEM is released.
+      tc::commit(&mma_done[w]);
+      mbar_wait(&mma_done[w], 0, p.status, PA_DEVICE_TIMEOUT_MMA);
     }
     __syncwarp();
-  } else if (warp == kSchedWarp) {
-    // ------------------------------------------------------------ scheduler
-    // Waits on every barrier the MMA issuer depends on, in the issuer's
-    // order, and releases it step by step (the same rendezvous sequence,
-    // so both warps pass named barrier 1 equally often on every path).
-    uint32_t li = 0, g = 0;
-    bool ok = true, aborted = false;
-    auto step = [&](bool wait_ok) {  // lane 0 waited; warp-wide release + vote
-      ok = __shfl_sync(0xffffffffu, ok && wait_ok && !*abort_flag, 0);
-      return rendezvous(!ok) != 0;
-    };
-    for (uint32_t cons = 0;; ++cons) {
-      int idx = -1, ntiles = 0;
-      bool w_ok = true;
-      if (lane == 0) {
-        const int rs = cons % L::kRing;
-        w_ok = ok && mbar_wait(&item_full[rs], (cons / L::kRing) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-        if (w_ok) {
-          idx = ring[rs];
-          mbar_arrive(&item_empty[rs]);
-          Item it;
-          if (idx >= 0 && item_at(p, idx, N, it)) ntiles = it.ntiles;
-          else idx = -1;
-        }
-        sched_box[0] = idx;
-        sched_box[1] = ntiles;
-      }
-      idx = __shfl_sync(0xffffffffu, idx, 0);
-      ntiles = __shfl_sync(0xffffffffu, ntiles, 0);
-      if (step(w_ok)) { aborted = true; break; }
-      if (idx < 0) break;
-      const int qb = li % QB;
-      for (int j = 0; j < ntiles && !aborted; ++j, ++g) {
-        const int st = g % ST;
-        if constexpr (L::kAliasP) {
-          // [P V(g-1) +] S(g) of group w: K(g) and Q in, P_w(g-1) written
-          // (so S_w(g-1) was read), O_w read out before the item's first P V.
-          // At j = 0 the previous item's last P_w was waited for at its tail.
-          for (int w = 0; w < 2 && !aborted; ++w) {
-            w_ok = true;
-            if (lane == 0) {
-              if (w == 0 && j == 0) w_ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-              if (w_ok && w == 0) w_ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-              if (L::kSplitKV && w_ok && w == 0 && j > 0)
-                w_ok = mbar_wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-              if (w_ok && j > 0) w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-              if (w_ok && j == 1 && li > 0)
-                w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-            }
-            if (step(w_ok)) aborted = true;
-          }
-        } else {
-          for (int w = 0; w < 2 && !aborted; ++w) {
-            w_ok = true;
-            if (lane == 0) {
-              if (w == 0 && j == 0) w_ok = mbar_wait(&q_full[qb], (li / QB) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-              if (w_ok && w == 0) w_ok = mbar_wait(&kv_full[st], (g / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-              if (w_ok && g > 0) w_ok = mbar_wait(&s_free[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-            }
-            if (step(w_ok)) aborted = true;
-          }
-          if (j > 0) {
-            for (int w = 0; w < 2 && !aborted; ++w) {
-              w_ok = true;
-              if (lane == 0) {
-                w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-                if (w_ok && j == 1 && li > 0)
-                  w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-              }
-              if (step(w_ok)) aborted = true;
-            }
-          }
-        }
-      }
-      if (aborted) break;
-      for (int w = 0; w < 2 && !aborted; ++w) {
-        w_ok = true;
-        if (lane == 0) {
-          if (L::kSplitKV && w == 0)
-            w_ok = mbar_wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-          if (w_ok) w_ok = mbar_wait(&p_full[w], (g - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-          if (w_ok && ntiles == 1 && li > 0)
-            w_ok = mbar_wait(&o_empty[w], (li - 1) & 1, p.status, PA_DEVICE_TIMEOUT_MMA);
-        }
-        if (step(w_ok)) aborted = true;
-      }
-      if (aborted) break;
-      ++li;
-    }
-    if (aborted && lane == 0) *abort_flag = 1;
   }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
@@ -659,7 +597,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const int nfull = (it.prefix + p0w + 1) / N;
       float m_run = -INFINITY, l = 0.f;
       for (int j = 0; j < it.ntiles; ++j, ++t) {
-        ok = mbar_wait(&s_full[w], t & 1, p.status, PA_DEVICE_TIMEOUT_MMA) && !*abort_flag;
+        constexpr bool kSpin = D == 64 ? PA_PREFILL_SPIN_SOFTMAX64 : PA_PREFILL_SPIN_SOFTMAX128;
+        ok = (kSpin ? mbar_wait_spin(&s_full[w], t & 1, p.status, PA_DEVICE_TIMEOUT_MMA)
+                    : mbar_wait(&s_full[w], t & 1, p.status, PA_DEVICE_TIMEOUT_MMA)) &&
+             !*abort_flag;
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc::fence_after_sync();
@@ -722,9 +663,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             }
           }
         }
-        if (w == 0 && j == it.ntiles - 1 && r < N) {
+        if (j == it.ntiles - 1 && r < N) {
           // V rows past the context (stale or poisoned slots of the last
           // block) are zeroed so 0-probability columns contribute exactly 0.
+          // Both groups zero them before their P is published: each M-tile's
+          // P V is issued by its own thread after its own group's zeroing,
+          // and the other group's stores write the same zero bytes.
           const int tok = j * N + r;
           if (tok >= it.ctx) {
             const int st = t % ST;
@@ -815,7 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == kMmaWarp) {
+  if (warp == kMmaWarp0) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, L::kTmemCols);
   }
