@@ -534,6 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             if (!ok) break;
             issue_s(qb, st);
             tc::commit(&kv_empty[st]);  // K(g)
+            if (j == ntiles - 1) tc::commit(&q_empty[qb]);  // the item's last read of Q_w
             if (w == 0) mbar_arrive(&turn[st]);
           } else {
             // S_w(g) once K(g) is in and the softmax has read S_w(g-1), then
@@ -541,6 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             if (g > 0) wait(&s_free[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
             if (!ok) break;
             issue_s(qb, st);
+            if (j == ntiles - 1) tc::commit(&q_empty[qb]);  // the item's last read of Q_w
             if (w == 0) mbar_arrive(&turn[st]);
             if (j > 0) {
               wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
@@ -552,14 +554,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           }
         }
         if (!ok) break;
-        // Last P V of the item, then release its K/V stage and Q buffer.
+        // Last P V of the item, then release its K/V stage (its Q buffer
+        // went with the last S).
         if (L::kSplitKV) wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, PA_DEVICE_TIMEOUT_TMA);
         wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
         if (ntiles == 1 && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
         if (!ok) break;
         issue_pv((g - 1) % ST, ntiles > 1, true);
         tc::commit(L::kSplitKV ? &v_empty[(g - 1) % ST] : &kv_empty[(g - 1) % ST]);
-        tc::commit(&q_empty[qb]);
         ++li;
       }
       if (!ok) *abort_flag = 1;
