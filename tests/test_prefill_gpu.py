@@ -152,6 +152,24 @@ def test_prefill_block_size_32(cuda_device):
     check(out, oracle_prefill(case), torch.bfloat16)
 
 
+@pytest.mark.parametrize("layout", ["units", "levels"])
+def test_schedule_past_the_order_table(cuda_device, layout):
+    """Work past the kernel's longest-first order table (more than 2048
+    (sequence, M-tile pair) units, or a chunk whose KV range spans 512 or
+    more 128-key tiles) keeps the schedule order; results are unchanged."""
+    if layout == "units":
+        rng = np.random.default_rng(21)
+        nseq = 2100  # 1 query head per KV head: 256 positions per unit, one unit per sequence
+        prefix = rng.integers(0, 40, size=nseq).tolist()
+        chunk = rng.integers(1, 4, size=nseq).tolist()
+        case = make_prefill_case(prefix, chunk, 8, 8, 64, 16, torch.bfloat16, cuda_device, seed=21, extra_blocks=1)
+    else:
+        case = make_prefill_case([66000, 3], [5, 40], 8, 1, 64, 16, torch.bfloat16, cuda_device, seed=22)
+    out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
+                                         case["max_q"])
+    check(out, oracle_prefill(case), torch.bfloat16)
+
+
 def test_static_schedule_without_control_block(cuda_device):
     """control = NULL: the kernel hands out items statically; same result as
     the dynamic schedule."""
