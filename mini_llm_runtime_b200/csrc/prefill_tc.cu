@@ -11,11 +11,12 @@
 // r % G), P = floor(128 / G) positions per tile (18 for a group of 7 -> 126
 // live rows), so every K/V tile staged from the paged pool feeds all G query
 // heads of both M-tiles.  The kernel is persistent (one CTA per SM).  Items
-// are listed by descending query position (longest key ranges first) and
-// handed out dynamically: the producer warp claims the next index from a
-// global counter (self-rewinding: the last CTA to finish zeroes it) and
-// publishes it through a small ring in shared memory to the other roles.
-// Without a control block the CTAs take every gridDim.x-th item instead.
+// are handed out longest first (by KV tile count; a counting sort of the
+// work units built in shared memory at start, or descending query position
+// past its capacity) and dynamically: the producer warp claims the next
+// index from a global counter (self-rewinding: the last CTA to finish zeroes
+// it) and publishes it through a small ring in shared memory to the other
+// roles.  Without a control block the CTAs take every gridDim.x-th claim.
 //
 // Warp roles (384 threads; setmaxnreg moves registers to the softmax):
 //   warp 8      TMA producer: the item's two Q tiles (3-D boxes {64, G, P}
@@ -139,7 +140,12 @@ struct Lay {
   static constexpr int kRing = 4;             // claimed item indices in flight
   static constexpr int kNumBars = 2 * QB + 5 * ST + 10 + 2 + 2 * kRing;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;  // tmem slot, abort flag, item ring
-  static constexpr size_t kSmem = 1024 + kOffMisc + 16 + 4 * kRing;
+  // Longest-first order of the work units (sequence x pair of M-tiles):
+  // unit codes sorted by KV tile count, the per-count offsets, and each
+  // sequence's chunk length and prefix.
+  static constexpr int kLptUnits = 2048, kLptLevels = 512, kLptSeqs = 512;
+  static constexpr int kOffLpt = kOffMisc + 16 + 4 * kRing;
+  static constexpr size_t kSmem = 1024 + kOffLpt + 4 * (kLptUnits + kLptLevels + 2 * kLptSeqs);
   // TMEM: 256 columns per M-tile w: S (N FP32 columns), P (N/2 columns of
   // packed 16-bit values) and O, each aligned to its width:
   //   D=64,  N=128: S [0,128)  P [128,192)  O [192,256)
@@ -246,6 +252,86 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
 
 template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b) { return MmaOp<T>::pack(a, b); }
 
+// KV tiles of the pair `pi` of a chunk (item_at's ntiles).
+__device__ __forceinline__ int pair_tiles(int prefix, int C, int pi, int P, int N) {
+  const int p0 = pi * 2 * P;
+  return (prefix + min(C, p0 + 2 * P) - 1) / N + 1;
+}
+
+// Warp-collective: sorts the units (sequence, pair) with query rows by KV
+// tile count, descending, into lpt[] (unit code pair * num_seqs + seq).
+// Each sequence's metadata is read from global memory once (one round of
+// loads) into seq_c / seq_pre; lvl[] holds the counts.  Returns the number
+// of claims (units x Hkv), or -1 (keep the query-position order) when the
+// batch exceeds the tables or has fewer than kLptMinSeqs sequences: with
+// few sequences the costliest units all belong to one of them, and the
+// CTAs starting on them together stream the same K/V lines in step, which
+// measured slower than the query-position order's mix of sequences.
+constexpr int kLptMinSeqs = 8;
+__device__ int build_lpt(const TcParams& p, int N, int max_units, int max_levels, int max_seqs, int* lpt, int* lvl,
+                         int* seq_c, int* seq_pre, int lane) {
+  if (p.num_seqs > max_seqs || p.num_seqs < kLptMinSeqs) return -1;
+  const int P2 = 2 * p.P;
+  int units = 0, top = 0;
+  for (int s = lane; s < p.num_seqs; s += 32) {
+    // item_at's checks: a sequence without query rows has no units.
+    const int64_t q0 = __ldg(p.cu_q + s);
+    const int64_t c = __ldg(p.cu_q + s + 1) - q0;
+    int64_t ctx = __ldg(p.context_lens + s);
+    if (ctx > p.ctx_cap) ctx = p.ctx_cap;
+    int C = 0, prefix = 0;
+    if (!(c <= 0 || c > ctx || q0 < 0 || q0 + c > p.total_q)) {
+      C = static_cast<int>(c);
+      prefix = static_cast<int>(ctx - c);
+      const int np = min((C + P2 - 1) / P2, p.pairs);  // the schedule covers p.pairs pairs
+      units += np;
+      top = max(top, pair_tiles(prefix, C, np - 1, p.P, N));
+    }
+    seq_c[s] = C;
+    seq_pre[s] = prefix;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    units += __shfl_xor_sync(0xffffffffu, units, o);
+    top = max(top, __shfl_xor_sync(0xffffffffu, top, o));
+  }
+  if (units > max_units || top >= max_levels || (int64_t)units * p.Hkv >= (int64_t(1) << 31)) return -1;
+  for (int l = lane; l <= top; l += 32) lvl[l] = 0;
+  __syncwarp();
+  // Counting sort: count per tile count, offsets (highest count first),
+  // then place.  Lanes take sequences and step through their pairs
+  // together, so units of equal count alternate between sequences (as in
+  // the query-position order): CTAs running at the same time then read
+  // different sequences' K/V.
+  auto for_units = [&](auto&& fn) {
+    for (int s = lane; s < p.num_seqs; s += 32) {
+      const int C = seq_c[s];
+      if (C == 0) continue;
+      const int np = min((C + P2 - 1) / P2, p.pairs);
+      for (int pi = 0; pi < np; ++pi) fn(s, pi, pair_tiles(seq_pre[s], C, pi, p.P, N));
+    }
+  };
+  for_units([&](int, int, int cost) { atomicAdd(&lvl[cost], 1); });
+  __syncwarp();
+  int carry = 0;  // lvl[l] := units costing more than l
+  for (int base = top; base >= 0; base -= 32) {
+    const int l = base - lane;
+    const int v = l >= 0 ? lvl[l] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
+    }
+    if (l >= 0) lvl[l] = carry + incl - v;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  __syncwarp();
+  for_units([&](int s, int pi, int cost) { lpt[atomicAdd(&lvl[cost], 1)] = pi * p.num_seqs + s; });
+  __syncwarp();
+  return units * p.Hkv;
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                                                 const __grid_constant__ CUtensorMap tmap_k,
@@ -337,6 +423,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     uint32_t pub = 0;        // item indices published to the ring
     int next_static = blockIdx.x;
     bool ok = true;
+    // Longest first: items are claimed in order of descending KV tile count
+    // (cost), so the last claims of the grid are the cheapest and the CTAs
+    // finish together.  A counting sort of the units (sequence, pair of
+    // M-tiles) by cost, in shared memory; claim c is unit lpt[c / Hkv],
+    // KV head c % Hkv.  Shapes past the table's capacity keep the schedule
+    // order (descending query position).
+    int* lpt = reinterpret_cast<int*>(smem + L::kOffLpt);
+    int* lvl = lpt + L::kLptUnits;
+    int* seq_c = lvl + L::kLptLevels;
+    int* seq_pre = seq_c + L::kLptSeqs;
+    const int n_claims =
+        build_lpt(p, N, L::kLptUnits, L::kLptLevels, L::kLptSeqs, lpt, lvl, seq_c, seq_pre, lane);
     for (;;) {
       // Claim the next item with query rows (dynamic: global counter;
       // static: every gridDim.x-th) and publish its index to the consumers.
@@ -349,6 +447,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           } else {
             c = next_static;
             next_static += gridDim.x;
+          }
+          if (n_claims >= 0) {
+            if (c >= n_claims) break;
+            const int unit = lpt[c / p.Hkv];
+            const int pair = unit / p.num_seqs, seq = unit - pair * p.num_seqs;
+            idx = (p.pairs - 1 - pair) * (p.num_seqs * p.Hkv) + seq * p.Hkv + (c - (c / p.Hkv) * p.Hkv);
+            break;
           }
           if (c >= p.num_items) break;
           Item probe;
@@ -469,14 +574,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const uint32_t o_tmem = tmem + w * L::kWgCols + L::kTmemO;
       // O_w (+)= P_w V(stage): P_w from TMEM (8 columns per K=16 step), V
       // from shared memory; one add per MMA (compile-time offsets).
-      auto issue_pv = [&](int stage, bool accumulate, bool signal) {
+      // K steps [k0, k1) of the tile (keys 16*k0 .. 16*k1-1).
+      auto issue_pv_steps = [&](int stage, bool accumulate, int k0, int k1) {
         tc::fence_after_sync();
         const uint32_t b0 = v_lo + stage * (L::kKVTile >> 4);
-        tc::mma_ts_words(o_tmem, p_tmem, b0, kHi, idesc_o, accumulate ? 1u : 0u);
 #pragma unroll
-        for (int kk = 1; kk < N / 16; ++kk)
-          tc::mma_ts_words(o_tmem, p_tmem + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o, 1u);
-        if (signal) tc::commit(&pv_done[w]);
+        for (int kk = 0; kk < N / 16; ++kk)
+          if (kk >= k0 && kk < k1)
+            tc::mma_ts_words(o_tmem, p_tmem + kk * 8, b0 + ((kk * 2048) >> 4), kHi, idesc_o,
+                             (accumulate || kk > 0) ? 1u : 0u);
       };
       // S_w = Q_w K(stage)^T, both from shared memory.
       auto issue_s = [&](int qb, int stage) {
@@ -499,6 +605,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         return ok;
       };
       uint32_t li = 0, g = 0;
+      // P_w(t) V(t) once P_w(t) is in TMEM (and O_w read out, for an item's
+      // first P V).
+      auto pv_when_ready = [&](uint32_t t, bool accumulate, bool first_of_item) {
+        wait(&p_full[w], t & 1, PA_DEVICE_TIMEOUT_MMA);
+        if (first_of_item && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
+        if (!ok) return false;
+        issue_pv_steps(t % ST, accumulate, 0, N / 16);
+        return true;
+      };
       for (uint32_t cons = 0; ok; ++cons) {
         const int rs = cons % L::kRing;
         if (!wait(&item_full[rs], (cons / L::kRing) & 1, PA_DEVICE_TIMEOUT_TMA)) break;
@@ -525,10 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             // holds the P V of tile g-1.
             if (j > 0) {
               wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, PA_DEVICE_TIMEOUT_TMA);
-              wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
-              if (j == 1 && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
-              if (!ok) break;
-              issue_pv((g - 1) % ST, j > 1, false);
+              if (!pv_when_ready(g - 1, j > 1, j == 1)) break;
               tc::commit(&v_empty[(g - 1) % ST]);
             }
             if (!ok) break;
@@ -545,10 +657,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
             if (j == ntiles - 1) tc::commit(&q_empty[qb]);  // the item's last read of Q_w
             if (w == 0) mbar_arrive(&turn[st]);
             if (j > 0) {
-              wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
-              if (j == 1 && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
-              if (!ok) break;
-              issue_pv((g - 1) % ST, j > 1, true);
+              if (!pv_when_ready(g - 1, j > 1, j == 1)) break;
+              tc::commit(&pv_done[w]);
               tc::commit(&kv_empty[(g - 1) % ST]);
             }
           }
@@ -557,10 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         // Last P V of the item, then release its K/V stage (its Q buffer
         // went with the last S).
         if (L::kSplitKV) wait(&v_full[(g - 1) % ST], ((g - 1) / ST) & 1, PA_DEVICE_TIMEOUT_TMA);
-        wait(&p_full[w], (g - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
-        if (ntiles == 1 && li > 0) wait(&o_empty[w], (li - 1) & 1, PA_DEVICE_TIMEOUT_MMA);
-        if (!ok) break;
-        issue_pv((g - 1) % ST, ntiles > 1, true);
+        if (!ok || !pv_when_ready(g - 1, ntiles > 1, ntiles == 1)) break;
+        tc::commit(&pv_done[w]);
         tc::commit(L::kSplitKV ? &v_empty[(g - 1) % ST] : &kv_empty[(g - 1) % ST]);
         ++li;
       }
@@ -692,6 +800,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const float2 negm2 = make_float2(-m_run, -m_run);
         float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         uint32_t pk[N / 2];  // P row, two 16-bit values per 32-bit TMEM column
+        const uint32_t p_addr = wg_addr + L::kTmemP;
 #pragma unroll
         for (int c = 0; c < N / 8; ++c) {
 #pragma unroll
@@ -711,7 +820,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
         ok = wait_pv();
         if (!ok) break;
-        const uint32_t p_addr = wg_addr + L::kTmemP;
 #pragma unroll
         for (int c = 0; c + 32 <= N / 2; c += 32) tc::tmem_st32(p_addr + c, pk + c);
         if ((N / 2) % 32) tc::tmem_st16(p_addr + (N / 2) / 32 * 32, pk + (N / 2) / 32 * 32);

@@ -154,9 +154,9 @@ def test_prefill_block_size_32(cuda_device):
 
 @pytest.mark.parametrize("layout", ["units", "levels"])
 def test_schedule_past_the_order_table(cuda_device, layout):
-    """Work past the kernel's longest-first order table (more than 2048
-    (sequence, M-tile pair) units, or a chunk whose KV range spans 512 or
-    more 128-key tiles) keeps the schedule order; results are unchanged."""
+    """Work past the kernel's longest-first order table (more than 512
+    sequences, or a chunk whose KV range spans 512 or more 128-key tiles)
+    keeps the query-position order; results are unchanged."""
     if layout == "units":
         rng = np.random.default_rng(21)
         nseq = 2100  # 1 query head per KV head: 256 positions per unit, one unit per sequence
@@ -164,7 +164,9 @@ def test_schedule_past_the_order_table(cuda_device, layout):
         chunk = rng.integers(1, 4, size=nseq).tolist()
         case = make_prefill_case(prefix, chunk, 8, 8, 64, 16, torch.bfloat16, cuda_device, seed=21, extra_blocks=1)
     else:
-        case = make_prefill_case([66000, 3], [5, 40], 8, 1, 64, 16, torch.bfloat16, cuda_device, seed=22)
+        # 8 sequences (the order table's minimum), one spanning 516 key tiles
+        case = make_prefill_case([66000, 3, 17, 100, 0, 250, 64, 9], [5, 40, 33, 1, 90, 7, 64, 2], 8, 1, 64, 16,
+                                 torch.bfloat16, cuda_device, seed=22)
     out = paged_attention_prefill_varlen(case["q"], case["cu"], case["lens"], case["tables"], case["k"], case["v"],
                                          case["max_q"])
     check(out, oracle_prefill(case), torch.bfloat16)
