@@ -37,6 +37,24 @@ from .qwen2_attention import check_decode_metadata, new_token_blocks_private
 
 class PagedDecodeGraph:
     COPY_CHUNK_LAYERS = 4  # layers per host<->device copy chunk (host I/O mode)
+    # The first chunk's inputs and the last chunk's outputs cannot overlap
+    # any kernel of the step, so those two chunks carry one layer each.
+    EDGE_CHUNK_LAYERS = 1
+
+    @classmethod
+    def copy_chunks(cls, num_layers: int) -> list[tuple[int, int]]:
+        """[first, last) layer ranges of the step's copy chunks."""
+        edge, mid = cls.EDGE_CHUNK_LAYERS, cls.COPY_CHUNK_LAYERS
+        if num_layers <= 2 * edge:
+            return [(a, min(a + edge, num_layers)) for a in range(0, num_layers, edge)]
+        chunks = [(0, edge)]
+        a = edge
+        while a < num_layers - edge:
+            b = min(a + mid, num_layers - edge)
+            chunks.append((a, b))
+            a = b
+        chunks.append((num_layers - edge, num_layers))
+        return chunks
 
     def __init__(
         self,
@@ -70,18 +88,26 @@ class PagedDecodeGraph:
         self.scale = (1.0 / math.sqrt(cache.head_dim)) if scale is None else float(scale)
         L, B, H, D, HKV = len(self.layers), batch, num_q_heads, cache.head_dim, cache.num_kv_heads
         dt = cache.dtype
-        self.q = torch.zeros(L, B, H, D, dtype=dt, device=dev)
-        self.new_k = torch.zeros(L, B, HKV, D, dtype=dt, device=dev)
-        self.new_v = torch.zeros(L, B, HKV, D, dtype=dt, device=dev)
-        self.slot_mapping = torch.zeros(B, dtype=torch.long, device=dev)
-        self.block_tables = torch.zeros(B, max_blocks, dtype=torch.long, device=dev)
-        self.context_lens = torch.ones(B, dtype=torch.long, device=dev)
+        # All of a step's inputs live in one byte buffer, the same layout on
+        # the device and (pinned) on the host: the metadata, then one record
+        # per layer [q | new_k | new_v], each 256-byte aligned.  A copy chunk
+        # is then one contiguous range, and the first one carries the
+        # metadata as well: one copy before the first layer can start.
+        es = torch.empty(0, dtype=dt).element_size()
+        align = lambda n: (n + 255) // 256 * 256  # noqa: E731
+        q_bytes, kv_bytes = B * H * D * es, B * HKV * D * es
+        self._meta_bytes = align(8 * (2 * B + B * max_blocks))
+        self._rec_bytes = align(q_bytes + 2 * kv_bytes)
+        total = self._meta_bytes + L * self._rec_bytes
+        self._stage_dev = torch.zeros(total, dtype=torch.uint8, device=dev)
+        self._dev_inputs = self._stage_views(self._stage_dev, L, B, H, HKV, D, max_blocks, dt)
+        self._dev_inputs["context_lens"].fill_(1)
+        self.q, self.new_k, self.new_v = (self._dev_inputs[k] for k in ("q", "new_k", "new_v"))
+        self.slot_mapping, self.block_tables, self.context_lens = (
+            self._dev_inputs[k] for k in ("slot_mapping", "block_tables", "context_lens"))
         self.out = torch.zeros(L, B, H, D, dtype=dt, device=dev)
-        self._dev_inputs = {
-            "q": self.q, "new_k": self.new_k, "new_v": self.new_v, "slot_mapping": self.slot_mapping,
-            "block_tables": self.block_tables, "context_lens": self.context_lens,
-        }
-        self.host_inputs = {k: torch.zeros(v.shape, dtype=v.dtype).pin_memory() for k, v in self._dev_inputs.items()}
+        self._stage_host = torch.zeros(total, dtype=torch.uint8).pin_memory()
+        self.host_inputs = self._stage_views(self._stage_host, L, B, H, HKV, D, max_blocks, dt)
         self.host_output = torch.zeros(self.out.shape, dtype=dt).pin_memory() if host_io else None
 
         lib = _lib.load()
@@ -100,33 +126,50 @@ class PagedDecodeGraph:
         self._d2h = torch.cuda.Stream(dev)
         self._capture()
 
+    def _stage_views(self, buf: torch.Tensor, L: int, B: int, H: int, HKV: int, D: int, W: int,
+                     dt: torch.dtype) -> dict:
+        """The named inputs as views of a staging buffer (layout in __init__)."""
+        i64 = buf.view(torch.int64)
+        el = buf.view(dt)
+        es = el.element_size()
+        rec, meta = self._rec_bytes // es, self._meta_bytes // es
+        q_el, kv_el = B * H * D, B * HKV * D
+        return {
+            "slot_mapping": i64[0:B],
+            "context_lens": i64[B:2 * B],
+            "block_tables": i64[2 * B:2 * B + B * W].view(B, W),
+            "q": torch.as_strided(el, (L, B, H, D), (rec, H * D, D, 1), meta),
+            "new_k": torch.as_strided(el, (L, B, HKV, D), (rec, HKV * D, D, 1), meta + q_el),
+            "new_v": torch.as_strided(el, (L, B, HKV, D), (rec, HKV * D, D, 1), meta + q_el + kv_el),
+        }
+
     # -- step body --------------------------------------------------------------
     def _body(self, stream: int, warm: bool = False) -> None:
         """Enqueue one step.  ``warm`` = eager first pass before capture: no
         copies and no KV writes (it must not modify the cache), decode only.
 
-        With host I/O the per-layer inputs travel in chunks of
-        ``COPY_CHUNK_LAYERS`` layers: the metadata and the first chunk on the
-        step's stream, the others on a side stream while the first layers
-        run, and each chunk's outputs go back on another side stream as soon
-        as its layers finish, so the copy engines work under the kernels."""
+        With host I/O the per-layer inputs travel in chunks (``copy_chunks``:
+        one layer first and last, ``COPY_CHUNK_LAYERS`` between): the
+        metadata and the first chunk on the step's stream, the others on a
+        side stream while the first layers run, and each chunk's outputs go
+        back on another side stream as soon as its layers finish, so the copy
+        engines work under the kernels."""
         lib, c = self._lib, self.cache
         B, H, D, HKV, bs = self.batch, self.hq, c.head_dim, c.num_kv_heads, c.block_size
         io = self.host_io and not warm
         main = torch.cuda.current_stream(self.device)
-        L, CH = len(self.layers), self.COPY_CHUNK_LAYERS
-        chunks = [(a, min(a + CH, L)) for a in range(0, L, CH)]
+        chunks = self.copy_chunks(len(self.layers))
         last_of_chunk = {b - 1: a for a, b in chunks}
         ready = {}
         if io:
-            for k in ("slot_mapping", "block_tables", "context_lens"):
-                self._dev_inputs[k].copy_(self.host_inputs[k], non_blocking=True)
-            self._h2d.wait_stream(main)
+            meta, rec = self._meta_bytes, self._rec_bytes
             for ci, (a, b) in enumerate(chunks):
+                lo, hi = (0 if ci == 0 else meta + a * rec), meta + b * rec
                 with torch.cuda.stream(main if ci == 0 else self._h2d):
-                    for k in ("q", "new_k", "new_v"):
-                        self._dev_inputs[k][a:b].copy_(self.host_inputs[k][a:b], non_blocking=True)
-                    if ci > 0:
+                    self._stage_dev[lo:hi].copy_(self._stage_host[lo:hi], non_blocking=True)
+                    if ci == 0:
+                        self._h2d.wait_stream(main)
+                    else:
                         ev = torch.cuda.Event()
                         ev.record(self._h2d)
                         ready[a] = ev
