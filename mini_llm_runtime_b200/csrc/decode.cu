@@ -254,7 +254,6 @@ struct FlatParams {
   int W;           // warps in the grid = slices
   float* part_ml;  // [W][2][16][2]   (m, l) of a slice's first / last cut piece
   float* part_o;   // [W][2][16][D]   unnormalised O of the same
-  int* prefix;     // [B + 1] per-sequence sub-block prefix sums (for the combine kernel)
   int* status;
   // Fused KV write (all null when the new token is already in the pools):
   // the new token's K/V rows [B, Hkv, D] (contiguous, pool dtype) replace the
@@ -361,8 +360,6 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
     if (b0 < p.B && b0 + per >= p.B) pre[p.B] = run;
   }
   __syncthreads();
-  if (blockIdx.x == 0)
-    for (int i = tid; i <= p.B; i += NT) p.prefix[i] = pre[i];
   const int64_t total = (int64_t)pre[p.B] * p.SPS;
   const int g = blockIdx.x * NW + warp;
   const int64_t lo = (int64_t)g * total / p.W, hi = (int64_t)(g + 1) * total / p.W;
@@ -923,8 +920,7 @@ DecodePlan plan_decode(int batch, int hkv, int hq, int D, int bs, int64_t bt_wid
     const size_t W = (size_t)pl.grid * flat_nw(D);
     const size_t ml = align256(sizeof(float) * 2 * 16 * 2 * W);
     const size_t po = align256(sizeof(float) * 2 * 16 * (size_t)D * W);
-    const size_t pre = align256(sizeof(int) * (size_t)(batch + 1));
-    pl.ws_bytes = 256 + tickets + ml + po + pre;
+    pl.ws_bytes = 256 + tickets + ml + po;
     return pl;
   }
   if (tc_shape_ok(dtype, D, bs)) {
@@ -1111,7 +1107,6 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
       const size_t po_bytes = align256(sizeof(float) * 2 * 16 * (size_t)head_dim * p.W);
       p.part_ml = reinterpret_cast<float*>(ws + off_ml);
       p.part_o = reinterpret_cast<float*>(ws + off_ml + ml_bytes);
-      p.prefix = reinterpret_cast<int*>(ws + off_ml + ml_bytes + po_bytes);
       p.status = status;
       p.new_k = fw ? fw->new_k : nullptr;
       p.new_v = fw ? fw->new_v : nullptr;
