@@ -71,9 +71,9 @@ static_assert(4 * 32 * kCtrlRegs + 8 * 32 * kSoftmaxRegs <= kThreads * 168, "reg
 constexpr float kRescaleLog2 = 8.f;          // lazy-rescale threshold (log2 units)
 constexpr int kBoxTokens = 16;               // tokens per K/V TMA box
 // Of every 8 column pairs of a score row, how many take the FMA-pipe exp2
-// (the rest the MUFU one).  head_dim 64 is bound by the exponentials and
-// gains from moving a quarter of them; head_dim 128 has twice the tensor
-// work per score and is not.
+// (the rest the MUFU one).  Measured best: a quarter at head_dim 64, where
+// the softmax is a larger share of each tile, none at head_dim 128 (twice
+// the tensor work per score).
 #ifndef PA_PREFILL_POLY64
 #define PA_PREFILL_POLY64 2
 #endif
