@@ -222,6 +222,9 @@ def _bf16_randn(shape, device, gen):
 
 
 def _decode_case(device, layers, ctx, hq, hkv, d, partition, seed):
+    """A decode kernel case: ``fn(l)`` runs layer l; ``inputs`` holds the
+    tensors (the parity tests run the oracle on them); ``work`` is the
+    algorithmic bytes of one launch."""
     from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel, paged_attention_decode_split_kv
 
     rng = np.random.default_rng(seed)
@@ -236,7 +239,9 @@ def _decode_case(device, layers, ctx, hq, hkv, d, partition, seed):
     else:
         fn = lambda l: paged_attention_decode_batch_parallel(q[l], k[l], v[l], bt, cl, BS)  # noqa: E731
     work = int(ctx.sum()) * hkv * d * 2 * 2 + 2 * len(ctx) * hq * d * 2 + int(((ctx + BS - 1) // BS).sum()) * 8
-    return fn, work
+    inputs = {"kind": "decode", "q": q, "k": k, "v": v, "tables": tables, "ctx": ctx, "block_tables": bt,
+              "context_lens": cl, "partition": partition}
+    return {"fn": fn, "work": work, "inputs": inputs}
 
 
 def _prefill_case(device, layers, prefix, chunk, hq, hkv, d, seed):
@@ -253,7 +258,9 @@ def _prefill_case(device, layers, prefix, chunk, hq, hkv, d, seed):
     bt, cl = torch.tensor(tables, device=device), torch.tensor(ctx, device=device)
     cmax = int(chunk.max())
     fn = lambda l: paged_attention_prefill_varlen(q[l], cu, cl, bt, k[l], v[l], cmax)  # noqa: E731
-    return fn, prefill_flops(prefix, chunk, hq, d)
+    inputs = {"kind": "prefill", "q": q, "k": k, "v": v, "tables": tables, "prefix": prefix, "chunk": chunk,
+              "ctx": ctx, "cu_q_lens": cu, "block_tables": bt, "context_lens": cl}
+    return {"fn": fn, "work": prefill_flops(prefix, chunk, hq, d), "inputs": inputs}
 
 
 def prefill_flops(prefix: np.ndarray, chunk: np.ndarray, hq: int, d: int) -> int:
@@ -311,7 +318,8 @@ def time_kernel_case(name: str, device, layers: int | None = None, reps: int | N
     build, bound, default_layers, desc = KERNEL_CASES[name]
     layers = layers or default_layers
     reps = reps or max(1, 64 // layers)
-    fn, work = build(device, layers)
+    case = build(device, layers)
+    fn, work = case["fn"], case["work"]
     for l in range(layers):
         fn(l)
     torch.cuda.synchronize()
@@ -329,7 +337,7 @@ def time_kernel_case(name: str, device, layers: int | None = None, reps: int | N
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / (reps * layers)
-    del graph
+    del graph, case, fn
     if bound == "hbm":
         peak, src = hbm_peak()
         achieved, unit = work / (ms * 1e-3) / 1e9, "GB/s"
