@@ -54,6 +54,9 @@ extern "C" {
 #define PA_DTYPE_BF16 2
 #define PA_DTYPE_F64 3
 
+/* Flags of pa_paged_decode_ex. */
+#define PA_DECODE_EARLY_INPUTS 1 /* metadata and pools may be read before the PDL wait */
+
 /* Ints in the control block of pa_chunk_prefill. */
 #define PA_PREFILL_CONTROL_INTS 4
 
@@ -120,11 +123,13 @@ PA_API size_t pa_decode_workspace_bytes(int batch, int num_kv_heads, int num_q_h
  * context_lens : [B] int64, includes the token being decoded (> 0)
  * out          : [B, Hq, D], element strides (o_s0, o_s1)
  * dtype        : F32, F16 or BF16 for q, pools and out (all the same)
- * partition_tokens : 0 = balanced split chosen by the library (BF16/F16,
- *                head_dim 64/128: the batch's KV is cut into one equal range
- *                per SM, ranges that cut a sequence are LSE-merged);
- *                > 0 = every sequence is cut into partitions of this many
- *                tokens (rounded up to a multiple of 16), LSE-merged.
+ * partition_tokens : BF16/F16 with head_dim 64/128 and batch <= 1024 take
+ *                the balanced kernel whatever its value: the batch's KV is
+ *                cut into equal ranges per CTA and the pieces of a sequence
+ *                are LSE-merged, so the value (accepted for the Triton
+ *                split-KV signature) changes nothing beyond FP32 rounding.
+ *                Elsewhere > 0 cuts every sequence into partitions of this
+ *                many tokens, LSE-merged; 0 lets the library choose.
  * workspace    : >= pa_decode_workspace_bytes(...) bytes, 256-byte aligned,
  *                see pa_decode_workspace_bytes for the zeroing rule.
  */
@@ -161,6 +166,33 @@ PA_API int pa_paged_decode_write(const void* q, int64_t q_s0, int64_t q_s1, cons
                           int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
                           int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, void* workspace,
                           size_t workspace_bytes, void* stream);
+
+/*
+ * pa_paged_decode and pa_paged_decode_write in one entry point, with flags.
+ * new_k, new_v and slot_mapping are all NULL (decode only, as
+ * pa_paged_decode, partition_tokens as there) or all set (the fused write of
+ * pa_paged_decode_write; partition_tokens must be 0).  Replaces the same
+ * reference pair as those two entry points
+ * (runtime/paged_kv_cache.py:194-249, kernels/reference/paged_attention.py:
+ * 178-254, as called by model/qwen2.py:608-621).
+ *
+ * flags = PA_DECODE_EARLY_INPUTS: the caller vouches that the kernel launched
+ * just before this call on `stream` (if any) writes none of context_lens,
+ * block_tables, slot_mapping or the pool rows other than the new tokens'.
+ * The balanced kernel then reads them (and starts its first K/V copies)
+ * before waiting for that kernel under programmatic dependent launch, so its
+ * start-up overlaps the previous kernel's tail — e.g. the previous layer's
+ * decode in a captured multi-layer step.  q, new_k and new_v are still read,
+ * and everything is written, only after the wait.  Without the flag the
+ * kernel waits before its first global access.
+ */
+PA_API int pa_paged_decode_ex(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k, const void* new_v,
+                              const int64_t* slot_mapping, void* k_pool_layer, void* v_pool_layer,
+                              int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                              const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
+                              const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
+                              int num_q_heads, float scale, int dtype, int partition_tokens, int flags,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * pa_paged_decode without a caller-supplied workspace: for callers that

@@ -21,6 +21,7 @@ PA_ERR_UNSUPPORTED = -2
 PA_ERR_CUDA = -3
 PA_ERR_WORKSPACE = -4
 PA_ERR_CAPACITY = -5
+PA_DECODE_EARLY_INPUTS = 1
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
 
@@ -50,6 +51,12 @@ SIGNATURES: dict[str, tuple] = {
         [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32,
          _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _f32, _i32, _c_void_p, _size,
          _c_void_p],
+    ),
+    "pa_paged_decode_ex": (
+        _i32,
+        [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32,
+         _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _f32, _i32, _i32, _i32, _c_void_p,
+         _size, _c_void_p],
     ),
     "pa_paged_decode_noalloc": (
         _i32,

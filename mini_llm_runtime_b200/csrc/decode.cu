@@ -5,30 +5,39 @@
 // split-KV pair (kernels/triton/paged_attention.py:528-700 stage 1,
 // :1530-1618 merge) to a ragged batch.
 //
-// Fast path (F16/BF16, head_dim 64 or 128, block_size % 16 == 0) — HBM-bound:
-//  * One CTA per (sequence, KV head, split of the context); the whole GQA
-//    group of that KV head (up to 16 query heads) rides on every K/V tile, so
-//    each K/V byte is read from HBM once per layer.
-//  * Each warp streams 16-token sub-blocks of the split (sub-block j of warp w
-//    is the split's sub-block w + j*NW).  Lane 0 looks the physical block up
-//    in the block table and issues two 3-D TMA boxes {64 dims, 1 head,
-//    16 tokens} (K and V, 128-byte swizzle) into the warp's ring of STAGES
-//    shared-memory stages, completing an mbarrier — one table load per
-//    sub-block, no per-token gathers.
+// Fast path (F16/BF16, head_dim 64 or 128, block_size % 16 == 0, batch <=
+// 1024) — HBM-bound: decode_flat_kernel, then decode_combine_kernel.
+//  * The batch's KV is one index space of 16-token sub-blocks ordered by
+//    (sequence, KV-head pack, position).  Each CTA owns an equal contiguous
+//    range of it and each warp an equal part of its CTA's range, so every SM
+//    streams the same number of bytes whatever the context lengths.
+//  * A warp streams its sub-blocks through its own TMA ring (3-D boxes
+//    {64 dims, 1 head, 16 tokens}, 128-byte swizzle, mbarrier completion),
+//    looking the physical block of each sub-block up in a lane-cached slice
+//    of the block table.
 //  * Scores S = Q K^T and O += P V use mma.sync m16n8k16 with FP32
-//    accumulators: rows are the group's query heads (padded to 16), so the
-//    per-token math costs ~1% of the CUDA-core budget and the kernel stays on
-//    the memory roofline.  Online softmax runs in FP32 in the log2 domain
-//    (scores pre-multiplied by scale*log2(e), exp2f).
-//  * Warps of a CTA are merged through shared memory; splits of a sequence
-//    are merged by the CTA that draws the last ticket (atomicAdd on a
-//    per-(seq, head-tile) counter, reset by that CTA).  No CTA ever waits for
-//    another one.
+//    accumulators.  When a GQA group has at most 8 query heads and the KV
+//    heads pair up, one warp serves two KV heads at once: rows 0-7 of the MMA
+//    hold the first head's query group and rows 8-15 the second's, and each
+//    head's K/V enter the MMA with the other half of the A operand zeroed.
+//    Every row of the tile then carries a real query head, so the online
+//    softmax does no work on padding rows.
+//  * Online softmax in FP32, log2 domain (scores pre-multiplied by
+//    scale * log2(e), exp2f).
+//  * A segment (one sequence x one KV-head pack) that lies inside one warp's
+//    range is finished by that warp.  Pieces of a segment cut by warp
+//    boundaries are merged by log-sum-exp in shared memory at the end of the
+//    CTA; a segment cut by CTA boundaries leaves one FP32 (m, l, O) record
+//    per CTA, merged by decode_combine_kernel, a second PDL launch.  No CTA
+//    waits for another one and nothing needs a memory fence: the kernel
+//    boundary orders the records before the combine reads them.
 // Tokens past context_len inside the last block are masked (-inf scores) and
 // their V fragments zeroed, so stale or NaN-poisoned slots cannot leak in.
 //
-// Everything else (F32, other head dims / block sizes) goes to the CUDA-core
-// kernel in attn_generic.cu.
+// decode_split_kernel serves batches above 1024 sequences (one CTA per
+// (sequence, KV head, partition), last-ticket merge).  Everything else (F32,
+// other head dims / block sizes) goes to the CUDA-core kernel in
+// attn_generic.cu.
 #include "attn_generic.cuh"
 
 namespace pa {
@@ -36,19 +45,33 @@ namespace {
 
 constexpr int kSub = 16;            // tokens per sub-block
 constexpr int kTileRowBytes = 128;  // one 64-wide column tile row (SW128 span)
-constexpr int kTileBytes = kSub * kTileRowBytes;  // 2 KB
+constexpr int kTileBytes = kSub * kTileRowBytes;  // 2 KB: 16 tokens x 64 dims of one head
 
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset inside a 64-col SW128 tile
   return static_cast<uint32_t>(row * kTileRowBytes + ((chunk ^ (row & 7)) << 4));
 }
 
-// Online-softmax state of one warp for one (sequence, KV head, head tile):
-// rows = up to 16 query heads of the GQA group (mma M dimension), FP32
-// (m, l) per row in the log2 domain and the FP32 O accumulator fragments.
-template <typename T, int D>
+// Query head (relative to the piece's first head) of MMA row r, or -1 for a
+// padding row.  PK = 2: rows 0-7 serve the first KV head's group, rows 8-15
+// the second's (group <= 8).  PK = 1: rows 0..hn-1 are consecutive heads.
+template <int PK>
+__device__ __forceinline__ int row_head(int r, int group, int hn) {
+  if (PK == 2) {
+    const int i = r & 7;
+    return i < group ? (r < 8 ? i : group + i) : -1;
+  }
+  return r < hn ? r : -1;
+}
+
+// Online-softmax state of one warp for one piece of a segment: 16 MMA rows
+// of query heads, FP32 (m, l) per row in the log2 domain and the FP32 O
+// accumulator fragments.  Shared-memory stage layout: tile t = (kv * kColTiles
+// + ct) * PK + h holds 16 tokens x 64 dims of KV head h of the pack (SW128).
+template <typename T, int D, int PK>
 struct WarpState {
   static constexpr int kKK = D / 16;  // k-steps of S = Q K^T
   static constexpr int kDT = D / 8;   // n-tiles of O = P V
+  static constexpr int kColTiles = D / 64;
   uint32_t qa[kKK][4];
   float m0, m1, l0, l1;
   float o[kDT][4];
@@ -60,26 +83,43 @@ struct WarpState {
     for (int i = 0; i < kDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   }
 
-  // A fragments of Q: rows h0 .. h0+hn-1 of q row qb (padded with zeros).
-  __device__ __forceinline__ void load_q(const T* qb, int64_t q_s1, int h0, int hn, int lane) {
-    const int r0 = lane >> 2, r1 = r0 + 8, cq = 2 * (lane & 3);
+  // A fragments of Q for rows r0 = lane/4 and r1 = r0 + 8 (zeros for padding).
+  __device__ __forceinline__ static void load_q(uint32_t (&qa_out)[kKK][4], const T* qb, int64_t q_s1, int h0,
+                                                int group, int hn, int lane) {
+    const int r0 = lane >> 2, cq = 2 * (lane & 3);
+    const int e0 = row_head<PK>(r0, group, hn), e1 = row_head<PK>(r0 + 8, group, hn);
+    const T* p0 = qb + (int64_t)(h0 + (e0 < 0 ? 0 : e0)) * q_s1;
+    const T* p1 = qb + (int64_t)(h0 + (e1 < 0 ? 0 : e1)) * q_s1;
 #pragma unroll
     for (int kk = 0; kk < kKK; ++kk) {
       const int c = kk * 16 + cq;
-      qa[kk][0] = r0 < hn ? load_pair_u32(qb + (int64_t)(h0 + r0) * q_s1 + c) : 0u;
-      qa[kk][1] = r1 < hn ? load_pair_u32(qb + (int64_t)(h0 + r1) * q_s1 + c) : 0u;
-      qa[kk][2] = r0 < hn ? load_pair_u32(qb + (int64_t)(h0 + r0) * q_s1 + c + 8) : 0u;
-      qa[kk][3] = r1 < hn ? load_pair_u32(qb + (int64_t)(h0 + r1) * q_s1 + c + 8) : 0u;
+      qa_out[kk][0] = e0 >= 0 ? load_pair_u32(p0 + c) : 0u;
+      qa_out[kk][1] = e1 >= 0 ? load_pair_u32(p1 + c) : 0u;
+      qa_out[kk][2] = e0 >= 0 ? load_pair_u32(p0 + c + 8) : 0u;
+      qa_out[kk][3] = e1 >= 0 ? load_pair_u32(p1 + c + 8) : 0u;
     }
   }
 
-  // NSUB 16-token sub-blocks staged at kb[u] / vb[u] (SW128 tiles); the
-  // first valid[u] tokens of sub-block u belong to the context.  Two
-  // sub-blocks per call give two independent MMA chains and one online-
-  // softmax rescale per 32 tokens.
+  // A operand of head h of the pack: PK = 2 keeps only that head's rows.
+  __device__ __forceinline__ static void head_rows(const uint32_t* a, int h, uint32_t* out) {
+    if (PK == 1) {
+      out[0] = a[0];
+      out[1] = a[1];
+      out[2] = a[2];
+      out[3] = a[3];
+    } else {
+      out[0] = h == 0 ? a[0] : 0u;
+      out[1] = h == 0 ? 0u : a[1];
+      out[2] = h == 0 ? a[2] : 0u;
+      out[3] = h == 0 ? 0u : a[3];
+    }
+  }
+
+  // NSUB 16-token sub-blocks staged at stage[u]; the first valid[u] tokens of
+  // sub-block u belong to the context.
   template <int NSUB>
-  __device__ __forceinline__ void consume(const uint32_t* kb, const uint32_t* vb, const int* valid, float scale_log2,
-                                          int lane) {
+  __device__ __forceinline__ void consume(const uint32_t* stage, const int* valid, float scale_log2, int lane) {
+    constexpr uint32_t kVOff = kColTiles * PK * kTileBytes;
     const int mi = lane >> 3, mr = lane & 7, cq = 2 * (lane & 3);
     float s[2 * NSUB][4];
 #pragma unroll
@@ -90,11 +130,16 @@ struct WarpState {
       const int row = (mi >> 1) * 8 + mr;
       const int chunk = 2 * kin + (mi & 1);
 #pragma unroll
-      for (int u = 0; u < NSUB; ++u) {
-        uint32_t b00, b01, b10, b11;
-        ldsm_x4(kb[u] + ct * kTileBytes + swz(row, chunk), b00, b01, b10, b11);
-        MmaOp<T>::run(s[2 * u], qa[kk], b00, b01);
-        MmaOp<T>::run(s[2 * u + 1], qa[kk], b10, b11);
+      for (int h = 0; h < PK; ++h) {
+        uint32_t a[4];
+        head_rows(qa[kk], h, a);
+#pragma unroll
+        for (int u = 0; u < NSUB; ++u) {
+          uint32_t b00, b01, b10, b11;
+          ldsm_x4(stage[u] + (ct * PK + h) * kTileBytes + swz(row, chunk), b00, b01, b10, b11);
+          MmaOp<T>::run(s[2 * u], a, b00, b01);
+          MmaOp<T>::run(s[2 * u + 1], a, b10, b11);
+        }
       }
     }
 #pragma unroll
@@ -153,32 +198,40 @@ struct WarpState {
       const uint32_t mlo = (cq < vu ? 0x0000ffffu : 0u) | (cq + 1 < vu ? 0xffff0000u : 0u);
       const uint32_t mhi = (cq + 8 < vu ? 0x0000ffffu : 0u) | (cq + 9 < vu ? 0xffff0000u : 0u);
 #pragma unroll
-      for (int dt = 0; dt < kDT; dt += 2) {
-        const int dtt = dt + (mi >> 1);
-        const int row = (mi & 1) * 8 + mr;
-        uint32_t v0, v1, v2, v3;
-        ldsm_x4_t(vb[u] + (dtt >> 3) * kTileBytes + swz(row, dtt & 7), v0, v1, v2, v3);
-        if (partial) {
-          v0 &= mlo;
-          v2 &= mlo;
-          v1 &= mhi;
-          v3 &= mhi;
+      for (int h = 0; h < PK; ++h) {
+        uint32_t ap[4];
+        head_rows(pa, h, ap);
+#pragma unroll
+        for (int dt = 0; dt < kDT; dt += 2) {
+          const int dtt = dt + (mi >> 1);
+          const int row = (mi & 1) * 8 + mr;
+          uint32_t v0, v1, v2, v3;
+          ldsm_x4_t(stage[u] + kVOff + ((dtt >> 3) * PK + h) * kTileBytes + swz(row, dtt & 7), v0, v1, v2, v3);
+          if (partial) {
+            v0 &= mlo;
+            v2 &= mlo;
+            v1 &= mhi;
+            v3 &= mhi;
+          }
+          MmaOp<T>::run(o[dt], ap, v0, v1);
+          MmaOp<T>::run(o[dt + 1], ap, v2, v3);
         }
-        MmaOp<T>::run(o[dt], pa, v0, v1);
-        MmaOp<T>::run(o[dt + 1], pa, v2, v3);
       }
     }
   }
 
-  // Row sums are spread over the 4 lanes of a quad; gather them, then write
-  // rows [0, 16) as records of kRec floats: {m, l, -, -, O[0..D)} (O starts
-  // 16-byte aligned so merges read it with float4 loads).
-  static constexpr int kRec = D + 4;
-  __device__ __forceinline__ void store(float* area, int lane) {
+  // Sum the row sums over the 4 lanes of a quad (rows are spread that way).
+  __device__ __forceinline__ void reduce_l() {
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  }
+
+  // Rows [0, 16) as records of kRec floats: {m, l, -, -, O[0..D)} (O starts
+  // 16-byte aligned so merges read it with float4 loads).  Call reduce_l first.
+  static constexpr int kRec = D + 4;
+  __device__ __forceinline__ void store(float* area, int lane) const {
     const int r0 = lane >> 2, r1 = r0 + 8, cq = 2 * (lane & 3);
     float* a0 = area + r0 * kRec;
     float* a1 = area + r1 * kRec;
@@ -195,25 +248,23 @@ struct WarpState {
       *reinterpret_cast<float2*>(a1 + c) = make_float2(o[dt][2], o[dt][3]);
     }
   }
-};
 
-// Merge `nw` warp records (m, l, O) of row h, column d (log2 domain).
-template <int D>
-__device__ __forceinline__ void merge_records(const float* area, int nw, int h, int d, float& m, float& l,
-                                              float& acc) {
-  constexpr int kRec = D + 4;
-  m = -INFINITY;
-  for (int w = 0; w < nw; ++w) m = fmaxf(m, area[(w * 16 + h) * kRec]);
-  l = 0.f;
-  acc = 0.f;
-  for (int w = 0; w < nw; ++w) {
-    const float* r = area + (w * 16 + h) * kRec;
-    if (r[0] == -INFINITY) continue;  // warp saw no token of this piece
-    const float sc = exp2f(r[0] - m);
-    l += sc * r[1];
-    acc += sc * r[4 + d];
+  // Final output of a piece that is a whole segment.  Call reduce_l first.
+  __device__ __forceinline__ void store_out(T* ob, int64_t o_s1, int h0, int group, int hn, int lane) const {
+    const int r0 = lane >> 2, cq = 2 * (lane & 3);
+    const int e0 = row_head<PK>(r0, group, hn), e1 = row_head<PK>(r0 + 8, group, hn);
+    const float i0 = 1.f / l0, i1 = 1.f / l1;
+#pragma unroll
+    for (int dt = 0; dt < kDT; ++dt) {
+      if (e0 >= 0)
+        *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e0) * o_s1 + dt * 8 + cq) =
+            MmaOp<T>::pack(o[dt][0] * i0, o[dt][1] * i0);
+      if (e1 >= 0)
+        *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e1) * o_s1 + dt * 8 + cq) =
+            MmaOp<T>::pack(o[dt][2] * i1, o[dt][3] * i1);
+    }
   }
-}
+};
 
 // Eight outputs of one row as a single 16-byte store.
 template <typename T>
@@ -226,18 +277,25 @@ __device__ __forceinline__ void store8(T* dst, const float* v, float scale) {
   *reinterpret_cast<int4*>(dst) = pk;
 }
 
+// acc[0..8) += wt * (v0, v1).
+__device__ __forceinline__ void axpy8(float wt, float4 v0, float4 v1, float* acc) {
+  acc[0] = fmaf(wt, v0.x, acc[0]);
+  acc[1] = fmaf(wt, v0.y, acc[1]);
+  acc[2] = fmaf(wt, v0.z, acc[2]);
+  acc[3] = fmaf(wt, v0.w, acc[3]);
+  acc[4] = fmaf(wt, v1.x, acc[4]);
+  acc[5] = fmaf(wt, v1.y, acc[5]);
+  acc[6] = fmaf(wt, v1.z, acc[6]);
+  acc[7] = fmaf(wt, v1.w, acc[7]);
+}
+
 // ===========================================================================
-// Balanced ("flattened") decode.  The batch's KV sub-blocks, ordered by
-// (sequence, KV head, head tile, position), form one index space of `total`
-// sub-blocks; warp g of the grid (W warps in all) owns the slice
-// [g*total/W, (g+1)*total/W).  A slice covers pieces of one or more
-// segments (segment = one sequence x KV head x head tile).  A segment inside
-// one slice is finished by its warp, which writes the output directly; the
-// segments cut by a slice's ends (at most its first and last piece) are
-// written as (m, l, O) partial records and merged by decode_combine_kernel.
-// Warps never wait for one another: no block barrier after the start-up
-// scan, no fences, no atomics — under a saturated memory system every such
-// round trip costs microseconds.
+// Balanced decode.  The sub-blocks of the batch, ordered by (sequence b,
+// segment x, position), form one index space of `total` sub-blocks, where a
+// segment is one KV-head pack (PK = 2: two KV heads; PK = 1: one KV head and
+// a tile of <= 16 of its query heads) of one sequence.  CTA c owns
+// [c*total/G, (c+1)*total/G); warp w of a CTA owns the w-th of NW equal parts
+// of it.
 // ===========================================================================
 constexpr int kFlatMaxBatch = 1024;
 
@@ -251,9 +309,9 @@ struct FlatParams {
   int64_t o_s0, o_s1;
   int B, Hq, Hkv, group, HT, SPS, bs;
   float scale_log2;
-  int W;           // warps in the grid = slices
-  float* part_ml;  // [W][2][16][2]   (m, l) of a slice's first / last cut piece
-  float* part_o;   // [W][2][16][D]   unnormalised O of the same
+  int grid;     // CTAs of the main kernel
+  int early;    // PA_DECODE_EARLY_INPUTS: read metadata and pools before the PDL wait
+  float* part;  // [grid][2][16][D + 4] records of segments shared with other CTAs
   int* status;
   // Fused KV write (all null when the new token is already in the pools):
   // the new token's K/V rows [B, Hkv, D] (contiguous, pool dtype) replace the
@@ -266,59 +324,111 @@ struct FlatParams {
   int64_t num_slots;
 };
 
-// Segment cursor over the flattened sub-block index space.
-struct SegCursor {
+// A segment's place in the index space.
+struct Seg {
   int b, segx;
   int64_t start, end;
-  __device__ __forceinline__ void seek(const int* pre, int B, int SPS, int64_t x) {
-    int lo = 0, hi = B - 1;  // largest b with pre[b] * SPS <= x
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if ((int64_t)pre[mid] * SPS <= x) lo = mid; else hi = mid - 1;
-    }
-    b = lo;
-    const int64_t base = (int64_t)pre[b] * SPS;
-    const int nsub = pre[b + 1] - pre[b];
-    segx = static_cast<int>((x - base) / nsub);
-    start = base + (int64_t)segx * nsub;
-    end = start + nsub;
-  }
 };
 
-template <int D, int NW, int STAGES>
+// The segment holding sub-block x (pre = per-sequence sub-block prefix sums).
+__device__ __forceinline__ Seg seg_at(const int* pre, int B, int SPS, int64_t x) {
+  int lo = 0, hi = B - 1;  // largest b with pre[b] * SPS <= x
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if ((int64_t)pre[mid] * SPS <= x) lo = mid; else hi = mid - 1;
+  }
+  Seg s;
+  s.b = lo;
+  const int64_t base = (int64_t)pre[lo] * SPS;
+  const int nsub = pre[lo + 1] - pre[lo];
+  s.segx = static_cast<int>((x - base) / nsub);
+  s.start = base + (int64_t)s.segx * nsub;
+  s.end = s.start + nsub;
+  return s;
+}
+
+__device__ __forceinline__ Seg seg_by_id(const int* pre, int SPS, int sid) {
+  Seg s;
+  s.b = sid / SPS;
+  s.segx = sid - s.b * SPS;
+  const int nsub = pre[s.b + 1] - pre[s.b];
+  s.start = (int64_t)pre[s.b] * SPS + (int64_t)s.segx * nsub;
+  s.end = s.start + nsub;
+  return s;
+}
+
+// First KV head, first query head and head count (PK = 1) of a segment.
+template <int PK>
+__device__ __forceinline__ void seg_heads(const FlatParams& p, int segx, int& kvh0, int& h0, int& hn) {
+  if (PK == 2) {
+    kvh0 = 2 * segx;
+    h0 = kvh0 * p.group;
+    hn = 2 * p.group;
+  } else {
+    const int kvh = segx / p.HT, ht = segx - kvh * p.HT;
+    kvh0 = kvh;
+    h0 = kvh * p.group + ht * 16;
+    hn = min(16, p.group - ht * 16);
+  }
+}
+
+template <int D, int PK, int NW, int STAGES>
 struct FlatCfg {
   static constexpr int kColTiles = D / 64;
-  static constexpr int kStageBytes = 2 * kColTiles * kTileBytes;  // K + V
+  static constexpr int kStageBytes = 2 * kColTiles * PK * kTileBytes;  // K + V of one sub-block
   static constexpr int kRingBytes = NW * STAGES * kStageBytes;
-  static constexpr int kRec = D + 4;                             // record floats per row
-  static constexpr int kStagingBytes = NW * 16 * kRec * 4;        // one 16-row record per warp
+  static constexpr int kRec = D + 4;  // record floats per row
+  static constexpr int kRecBytes = 16 * kRec * 4;
+  static constexpr int kStagingBytes = NW * kRecBytes;  // first-piece record per warp
   static constexpr int kPrefixBytes = (kFlatMaxBatch + 1) * 4;
   static constexpr int kOffStaging = kRingBytes;
   static constexpr int kOffPrefix = kOffStaging + kStagingBytes;
   static constexpr int kOffBars = kOffPrefix + ((kPrefixBytes + 15) & ~15);
   static constexpr size_t kSmem = 1024 + kOffBars + NW * STAGES * 8 + 64;
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
+  static_assert(STAGES * kStageBytes >= kRecBytes, "a warp's ring holds its last-piece record at the end");
 };
 
-template <typename T, int D, int NW, int STAGES, int CTAS>
+template <typename T, int D, int PK, int NW, int STAGES, int NSUB, int CTAS>
 __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                                                    const __grid_constant__ CUtensorMap tmap_v,
                                                                    FlatParams p) {
-  using C = FlatCfg<D, NW, STAGES>;
-  static_assert(STAGES >= 2, "pairs of sub-blocks are consumed together");
+  using C = FlatCfg<D, PK, NW, STAGES>;
+  using WS = WarpState<T, D, PK>;
+  static_assert(STAGES >= NSUB, "a consume step takes NSUB staged sub-blocks");
   constexpr int NT = NW * 32;
   constexpr int kRec = C::kRec;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* staging = reinterpret_cast<float*>(smem + C::kOffStaging);
   int* pre = reinterpret_cast<int*>(smem + C::kOffPrefix);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
   __shared__ int warp_sums[NW];
+  __shared__ int ent_seg[2 * NW];  // segment id of warp w's cut first (2w) / last (2w+1) piece, or -1
+  __shared__ int run_first[2 * NW], run_last[2 * NW], run_sid[2 * NW];
+  __shared__ int nruns_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint8_t* ring = smem + warp * STAGES * C::kStageBytes;
+  uint64_t* wbar = bars + warp * STAGES;
+  // Shared-memory set-up needs no global data: it overlaps the previous
+  // kernel under programmatic dependent launch.
+  if (lane == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&wbar[s], 1);
+    fence_barrier_init();
+  }
+  if (tid == 0) {
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
   const int64_t cap = p.bt_width * (int64_t)p.bs;
-  // Launched with PDL: wait for the previous kernel before touching global
-  // memory; let the combine kernel (and the next PDL kernel) launch early.
-  grid_dep_wait();
+  // Wait for the previous kernel before touching global memory — or, when the
+  // caller vouches that it writes none of the metadata and pools
+  // (PA_DECODE_EARLY_INPUTS), only before the first read of q / new_k /
+  // new_v and the first write, so the start-up (scan, block-table loads, the
+  // first TMA copies) overlaps the previous kernel's tail.  Let the next PDL
+  // kernel launch early either way (it waits for this one).
+  if (!p.early) grid_dep_wait();
   grid_dep_launch();
 
   // ---- prefix sums of per-sequence sub-block counts (block-wide scan) ----
@@ -361,318 +471,375 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
   }
   __syncthreads();
   const int64_t total = (int64_t)pre[p.B] * p.SPS;
-  const int g = blockIdx.x * NW + warp;
-  const int64_t lo = (int64_t)g * total / p.W, hi = (int64_t)(g + 1) * total / p.W;
-  if (lo >= hi) return;  // empty slice (only when total < W); no block barrier follows
-  const int nj = static_cast<int>(hi - lo);  // this warp's sub-blocks, contiguous
-
-  uint8_t* ring = smem + warp * STAGES * C::kStageBytes;
-  float* staging = reinterpret_cast<float*>(smem + C::kOffStaging) + warp * 16 * kRec;
-  uint64_t* wbar = bars + warp * STAGES;
-  if (lane == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(&wbar[s], 1);
-    fence_barrier_init();
-    prefetch_tensormap(&tmap_k);
-    prefetch_tensormap(&tmap_v);
+  // With fewer sub-blocks than CTAs, the first `total` CTAs take one each.
+  const int G = static_cast<int>(total < (int64_t)gridDim.x ? total : (int64_t)gridDim.x);
+  const int c = blockIdx.x;
+  if (c >= G) {  // whole CTA, before any further barrier
+    if (p.early) grid_dep_wait();
+    return;
   }
-  __syncwarp();
+  const int64_t clo = (int64_t)c * total / G, chi = (int64_t)(c + 1) * total / G;
+  const int64_t lo = clo + (chi - clo) * warp / NW, hi = clo + (chi - clo) * (warp + 1) / NW;
+  const int nj = static_cast<int>(hi - lo);  // this warp's sub-blocks
 
-  // Lane i caches the TMA row coordinate and KV head of sub-block tb + i of
-  // the slice, so a TMA issue never waits on a block-table load.
-  int tb = -32, my_y = 0, my_kvh = 0;
+  // Lane i caches the TMA row coordinate and first KV head of sub-block
+  // tb + i of the slice, so a TMA issue never waits on a block-table load.
+  int tb = -32, my_y = 0, my_kv = 0;
   auto refill = [&](int j) {  // warp-uniform
     tb = j & ~31;
     const int jj = tb + lane;
     if (jj < nj) {
       const int64_t xx = lo + jj;
-      SegCursor cur;
-      cur.seek(pre, p.B, p.SPS, xx);
-      const int64_t tok0 = (xx - cur.start) * kSub;
-      const int64_t pb = p.bt[(int64_t)cur.b * p.bt_stride + tok0 / p.bs];
+      const Seg s = seg_at(pre, p.B, p.SPS, xx);
+      const int tok0 = static_cast<int>(xx - s.start) * kSub;
+      const int64_t pb = p.bt[(int64_t)s.b * p.bt_stride + tok0 / p.bs];
       my_y = static_cast<int>(pb * p.bs + tok0 % p.bs);
-      my_kvh = cur.segx / p.HT;
+      int kvh0, h0, hn;
+      seg_heads<PK>(p, s.segx, kvh0, h0, hn);
+      my_kv = kvh0;
     }
   };
   auto issue = [&](int j) {  // warp-uniform call, lane 0 issues
     if (j >= tb + 32) refill(j);
     const int y = __shfl_sync(0xffffffffu, my_y, j & 31);
-    const int kvh = __shfl_sync(0xffffffffu, my_kvh, j & 31);
+    const int kv = __shfl_sync(0xffffffffu, my_kv, j & 31);
     if (lane == 0) {
       const int stage = j % STAGES;
       uint8_t* st = ring + stage * C::kStageBytes;
       mbar_arrive_expect_tx(&wbar[stage], C::kStageBytes);
 #pragma unroll
-      for (int ct = 0; ct < C::kColTiles; ++ct) {
-        tma_load_3d(st + ct * kTileBytes, &tmap_k, &wbar[stage], ct * 64, kvh, y);
-        tma_load_3d(st + (C::kColTiles + ct) * kTileBytes, &tmap_v, &wbar[stage], ct * 64, kvh, y);
-      }
+      for (int ct = 0; ct < C::kColTiles; ++ct)
+#pragma unroll
+        for (int h = 0; h < PK; ++h) {
+          tma_load_3d(st + (ct * PK + h) * kTileBytes, &tmap_k, &wbar[stage], ct * 64, kv + h, y);
+          tma_load_3d(st + ((C::kColTiles + ct) * PK + h) * kTileBytes, &tmap_v, &wbar[stage], ct * 64, kv + h, y);
+        }
     }
   };
-  for (int j = 0; j < STAGES && j < nj; ++j) issue(j);
+  int issued = 0;
+  for (; issued < STAGES && issued < nj; ++issued) issue(issued);
+  if (p.early) grid_dep_wait();
 
   const T* qbase = reinterpret_cast<const T*>(p.q);
   T* out = reinterpret_cast<T*>(p.out);
-  WarpState<T, D> ws;
+  WS ws;
   int jc = 0;  // sub-blocks of this slice consumed so far
   bool ok = true;
-  SegCursor pc;
-  pc.seek(pre, p.B, p.SPS, lo);
-  {
-    const int kvh = pc.segx / p.HT, ht = pc.segx - kvh * p.HT;
-    ws.load_q(qbase + (int64_t)pc.b * p.q_s0, p.q_s1, kvh * p.group + ht * 16, min(16, p.group - ht * 16), lane);
+  int first_sid = -1, last_sid = -1;
+  Seg pc{};
+  if (nj > 0) {
+    pc = seg_at(pre, p.B, p.SPS, lo);
+    int kvh0, h0, hn;
+    seg_heads<PK>(p, pc.segx, kvh0, h0, hn);
+    WS::load_q(ws.qa, qbase + (int64_t)pc.b * p.q_s0, p.q_s1, h0, p.group, hn, lane);
   }
   int64_t x = lo;
   while (x < hi) {
     const int b = pc.b, segx = pc.segx;
-    const int kvh = segx / p.HT, ht = segx - kvh * p.HT;
-    const int h0 = kvh * p.group + ht * 16, hn = min(16, p.group - ht * 16);
+    int kvh0, h0, hn;
+    seg_heads<PK>(p, segx, kvh0, h0, hn);
     const int64_t pend = min(pc.end, hi);
     const bool whole = pc.start >= lo && pc.end <= hi;
-    const int slot = (x == lo) ? 0 : 1;
     int64_t ctx = p.context_lens[b];
     ctx = ctx > cap ? cap : ctx;
     // The next piece's Q fragments load while this piece streams.
-    SegCursor nc = pc;
-    uint32_t qn[WarpState<T, D>::kKK][4];
+    Seg nc = pc;
+    uint32_t qn[WS::kKK][4];
     if (pend < hi) {
-      nc.seek(pre, p.B, p.SPS, pend);
-      const int kvn = nc.segx / p.HT, htn = nc.segx - kvn * p.HT;
-      const int h0n = kvn * p.group + htn * 16, hnn = min(16, p.group - htn * 16);
-      const T* qb = qbase + (int64_t)nc.b * p.q_s0;
-      const int r0 = lane >> 2, r1 = r0 + 8, cq = 2 * (lane & 3);
-#pragma unroll
-      for (int kk = 0; kk < WarpState<T, D>::kKK; ++kk) {
-        const int cc = kk * 16 + cq;
-        qn[kk][0] = r0 < hnn ? load_pair_u32(qb + (int64_t)(h0n + r0) * p.q_s1 + cc) : 0u;
-        qn[kk][1] = r1 < hnn ? load_pair_u32(qb + (int64_t)(h0n + r1) * p.q_s1 + cc) : 0u;
-        qn[kk][2] = r0 < hnn ? load_pair_u32(qb + (int64_t)(h0n + r0) * p.q_s1 + cc + 8) : 0u;
-        qn[kk][3] = r1 < hnn ? load_pair_u32(qb + (int64_t)(h0n + r1) * p.q_s1 + cc + 8) : 0u;
-      }
+      nc = seg_at(pre, p.B, p.SPS, pend);
+      int kvn, h0n, hnn;
+      seg_heads<PK>(p, nc.segx, kvn, h0n, hnn);
+      WS::load_q(qn, qbase + (int64_t)nc.b * p.q_s0, p.q_s1, h0n, p.group, hnn, lane);
     }
     ws.reset();
     const int jend = static_cast<int>(pend - lo);
     while (jc < jend) {
-      const int n = (jend - jc >= 2) ? 2 : 1;
-      uint32_t kb[2], vb[2];
-      int valid[2];
+      const int n = (jend - jc >= NSUB) ? NSUB : 1;
+      uint32_t stg[NSUB];
+      int valid[NSUB];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < NSUB; ++u) {
         if (u < n) {
           const int j = jc + u;
           const int stage = j % STAGES;
           if (ok) ok = mbar_wait(&wbar[stage], (j / STAGES) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-          kb[u] = smem_u32(ring + stage * C::kStageBytes);
-          vb[u] = kb[u] + C::kColTiles * kTileBytes;
+          stg[u] = smem_u32(ring + stage * C::kStageBytes);
           const int64_t sub = lo + j - pc.start;
           valid[u] = static_cast<int>(min((int64_t)kSub, ctx - sub * kSub));
           if (p.new_k != nullptr && (sub + 1) * kSub >= ctx) {
             // Fused KV write: the sub-block holding the new token (position
             // ctx - 1) gets its K/V rows from new_k / new_v in place of the
-            // pool's, and the head-tile-0 warp stores them to the pools.
-            // Lane i moves one 16-byte chunk: K then V, 64-column tiles,
-            // 8 chunks per 128-byte row (the TMA's 128-byte swizzle).
+            // pool's, and they are stored to the pools (by the head-tile-0
+            // segment when PK = 1).  One 16-byte chunk per lane and step:
+            // (K/V, column tile, head of the pack, chunk of the 128-byte row).
             const int r = static_cast<int>(ctx - 1 - sub * kSub);
-            constexpr int kChunks = 2 * C::kColTiles * 8;
-            if (lane < kChunks) {
-              const int kv = lane / (C::kColTiles * 8), rem = lane - kv * (C::kColTiles * 8);
-              const int ct = rem >> 3, c = rem & 7;
-              const int64_t src = ((int64_t)b * p.Hkv + kvh) * D + ct * 64 + c * 8;
-              const int4 val = __ldg(reinterpret_cast<const int4*>(
-                  reinterpret_cast<const T*>(kv ? p.new_v : p.new_k) + src));
-              uint8_t* dst = ring + stage * C::kStageBytes + (kv * C::kColTiles + ct) * kTileBytes + r * 128 +
-                             ((c ^ (r & 7)) << 4);
+            constexpr int kChunks = 2 * C::kColTiles * PK * 8;
+            const bool store_pool = PK == 2 || segx % p.HT == 0;
+            const int64_t slot = p.slots[b];
+            for (int i = lane; i < kChunks; i += 32) {
+              const int cc = i & 7, t = i >> 3;  // t = (kv * kColTiles + ct) * PK + h
+              const int h = t % PK, kvct = t / PK;
+              const int kv = kvct / C::kColTiles, ct = kvct - kv * C::kColTiles;
+              const int64_t src = ((int64_t)b * p.Hkv + kvh0 + h) * D + ct * 64 + cc * 8;
+              const int4 val =
+                  __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const T*>(kv ? p.new_v : p.new_k) + src));
+              uint8_t* dst = ring + stage * C::kStageBytes + t * kTileBytes + r * 128 + ((cc ^ (r & 7)) << 4);
               *reinterpret_cast<int4*>(dst) = val;
-              const int64_t slot = p.slots[b];
-              if (ht == 0 && slot >= 0 && slot < p.num_slots)
+              if (store_pool && slot >= 0 && slot < p.num_slots)
                 *reinterpret_cast<int4*>(reinterpret_cast<T*>(kv ? p.v_pool : p.k_pool) +
-                                         (slot * p.Hkv + kvh) * D + ct * 64 + c * 8) = val;
-              fence_proxy_async_smem();  // before the stage is refilled by TMA
+                                         (slot * p.Hkv + kvh0 + h) * D + ct * 64 + cc * 8) = val;
             }
+            fence_proxy_async_smem();  // before the stage is refilled by TMA
             __syncwarp();
           }
         }
       }
-      if (n == 2) ws.template consume<2>(kb, vb, valid, p.scale_log2, lane);
-      else ws.template consume<1>(kb, vb, valid, p.scale_log2, lane);
+      if (!ok) break;
+      if (n == NSUB) ws.template consume<NSUB>(stg, valid, p.scale_log2, lane);
+      else ws.template consume<1>(stg, valid, p.scale_log2, lane);
       __syncwarp();
       for (int u = 0; u < n; ++u)
-        if (jc + u + STAGES < nj) issue(jc + u + STAGES);
+        if (issued < nj) issue(issued++);
       jc += n;
     }
-    // Finish the piece: stage the record in this warp's shared memory, then
-    // write it with 16-byte stores (final output, or a partial record).
-    ws.store(staging, lane);
-    __syncwarp();
-    float* pml = p.part_ml + ((int64_t)(g * 2 + slot) * 16) * 2;
-    float* po = p.part_o + ((int64_t)(g * 2 + slot) * 16) * D;
-    for (int i = lane; i < hn * (D / 8); i += 32) {
-      const int h = i / (D / 8), d = 8 * (i - h * (D / 8));
-      const float* r = staging + h * kRec;
-      const float4 v0 = *reinterpret_cast<const float4*>(r + 4 + d);
-      const float4 v1 = *reinterpret_cast<const float4*>(r + 8 + d);
-      if (whole) {
-        const float vals[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d, vals, 1.f / r[1]);
-      } else {
-        *reinterpret_cast<float4*>(po + h * D + d) = v0;
-        *reinterpret_cast<float4*>(po + h * D + d + 4) = v1;
-      }
+    if (!ok) break;
+    ws.reduce_l();
+    if (whole) {
+      ws.store_out(out + (int64_t)b * p.o_s0, p.o_s1, h0, p.group, hn, lane);
+    } else if (x == lo) {  // cut at the slice start: park the record until the end
+      ws.store(staging + warp * 16 * kRec, lane);
+      first_sid = b * p.SPS + segx;
+    } else {  // cut at the slice end: the last piece, kept in registers
+      last_sid = b * p.SPS + segx;
     }
-    if (!whole && lane < hn) *reinterpret_cast<float2*>(pml + lane * 2) = make_float2(staging[lane * kRec], staging[lane * kRec + 1]);
-    __syncwarp();
     x = pend;
     if (x < hi) {
       pc = nc;
 #pragma unroll
-      for (int kk = 0; kk < WarpState<T, D>::kKK; ++kk)
+      for (int kk = 0; kk < WS::kKK; ++kk)
 #pragma unroll
         for (int e = 0; e < 4; ++e) ws.qa[kk][e] = qn[kk][e];
     }
   }
+  if (!ok) {
+    // A bounded wait gave up (status already recorded): wait, again bounded,
+    // for this warp's copies still in flight so none lands after the CTA has
+    // exited; the outputs are garbage and the status word says so.
+    for (int j = jc; j < issued; ++j) mbar_wait(&wbar[j % STAGES], (j / STAGES) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
+    first_sid = last_sid = -1;
+  }
+  // This warp's copies have all landed: its ring is free for the last-piece
+  // record.
+  if (last_sid >= 0) ws.store(reinterpret_cast<float*>(ring), lane);
+  if (lane == 0) {
+    ent_seg[2 * warp] = first_sid;
+    ent_seg[2 * warp + 1] = last_sid;
+  }
+  __syncthreads();
+
+  // ---- merge the pieces cut by warp boundaries (shared memory) -----------
+  // Entries in order (warp, first/last) form runs of equal segments.  A run
+  // whose segment lies inside this CTA's range is merged to the output;
+  // otherwise to this CTA's record of the segment in global memory — slot 0
+  // when the segment starts before the range, else slot 1 — which
+  // decode_combine_kernel merges with the other CTAs' records.
+  if (tid == 0) {
+    int n = 0, prev = -1;
+    for (int f = 0; f < 2 * NW; ++f) {
+      const int sid = ent_seg[f];
+      if (sid < 0) continue;
+      if (sid != prev) {
+        run_first[n] = f;
+        run_sid[n] = sid;
+        ++n;
+        prev = sid;
+      }
+      run_last[n - 1] = f;
+    }
+    nruns_s = n;
+  }
+  __syncthreads();
+  auto rec_row = [&](int f, int r) -> const float* {  // entry f's record, row r
+    return ((f & 1) ? reinterpret_cast<const float*>(smem + (f >> 1) * STAGES * C::kStageBytes)
+                    : staging + (f >> 1) * 16 * kRec) +
+           r * kRec;
+  };
+  constexpr int kItems = 16 * (D / 8);  // (row, 8 columns)
+  const int nruns = nruns_s;
+  for (int w = tid; w < nruns * kItems; w += NT) {
+    const int ri = w / kItems, it = w - ri * kItems;
+    const int sid = run_sid[ri], f0 = run_first[ri], f1 = run_last[ri];
+    const int r = it / (D / 8), d = 8 * (it - r * (D / 8));
+    const Seg S = seg_by_id(pre, p.SPS, sid);
+    int kvh0, h0, hn;
+    seg_heads<PK>(p, S.segx, kvh0, h0, hn);
+    const int hh = row_head<PK>(r, p.group, hn);
+    if (hh < 0) continue;
+    // Two passes (the maximum, then independent weighted sums) keep the
+    // records' contributions free of a serial rescale chain.
+    float mx = -INFINITY;
+    for (int f = f0; f <= f1; ++f)
+      if (ent_seg[f] == sid) mx = fmaxf(mx, rec_row(f, r)[0]);
+    float l = 0.f;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int f = f0; f <= f1; ++f) {
+      if (ent_seg[f] != sid) continue;
+      const float* rec = rec_row(f, r);
+      const float wt = exp2f(rec[0] - mx);
+      l = fmaf(wt, rec[1], l);
+      axpy8(wt, *reinterpret_cast<const float4*>(rec + 4 + d), *reinterpret_cast<const float4*>(rec + 8 + d), acc);
+    }
+    if (S.start >= clo && S.end <= chi) {
+      store8<T>(out + (int64_t)S.b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d, acc, 1.f / l);
+    } else {
+      float* row = p.part + (((int64_t)c * 2 + (S.start < clo ? 0 : 1)) * 16 + r) * kRec;
+      if (d == 0) *reinterpret_cast<float2*>(row) = make_float2(mx, l);
+      *reinterpret_cast<float4*>(row + 4 + d) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(row + 8 + d) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
 }
 
-// Second stage of the balanced decode: every segment (sequence x KV head x
-// head tile) cut by slice ends is merged (log-sum-exp) from the partial
-// records of the warps g0..g1 owning its first / last sub-block; warps with
-// an empty slice (only when the batch has fewer sub-blocks than warps) hold
-// none.  One CTA of 256 threads per segment; segments finished inside one
-// slice return at once.  Launched with PDL right behind the main kernel; the
-// loads of one stage are issued together so a merge costs a few round trips.
-constexpr int kCombineThreads = 256;
-// At most 64 registers (4 CTAs' worth per SM): a combine CTA then fits beside
-// the two main-kernel CTAs of an SM (2 x 128 threads x 188 registers), so the
-// PDL launch makes it resident early and only the record loads remain after
-// the main kernel ends.
+// Second stage of the balanced decode: segments cut by CTA boundaries.  CTA
+// (segment, slab of kCombineRows rows) merges the records that CTAs c0..c1
+// of the main kernel wrote for the segment; segments that one CTA finished
+// return at once.  Launched with PDL right behind the main kernel: the
+// segment's bounds come from the context lengths (an input the main kernel
+// does not write) before the wait, so only the record loads remain after it.
+constexpr int kCombineThreads = 128;
+constexpr int kCombineRows = 4;
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kCombineThreads, 4) decode_combine_kernel(FlatParams p) {
+template <typename T, int D, int PK>
+__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatParams p) {
+  constexpr int kRec = D + 4;
+  constexpr int kItems = kCombineRows * (D / 8);  // (row, 8 columns) per CTA
+  constexpr int kStripes = kCombineThreads / kItems;
+  static_assert(kStripes >= 1 && kCombineThreads % kItems == 0, "combine layout");
   __shared__ float sm_m[kCombineThreads], sm_l[kCombineThreads];
-  __shared__ float red[kCombineThreads * 8];
+  __shared__ float4 sm_acc[kCombineThreads][2];
   __shared__ int wsum[2][kCombineThreads / 32];
-  const int seg = blockIdx.x;
-  const int b = seg / p.SPS, segx = seg - b * p.SPS;
-  // The slice boundaries follow from the context lengths alone, an input
-  // the main kernel does not write: recompute this sequence's sub-block
-  // offset and the batch total before waiting for the main kernel (PDL), so
-  // only the record loads remain after the wait.
-  int pb0, nsub, ptot;
-  {
-    const int64_t cap = p.bt_width * (int64_t)p.bs;
-    int before = 0, all = 0;
-    for (int i = threadIdx.x; i < p.B; i += kCombineThreads) {
-      int64_t ctx = p.context_lens[i];
-      ctx = ctx > cap ? cap : ctx;
-      const int c = ctx > 0 ? static_cast<int>((ctx + kSub - 1) / kSub) : 0;
-      all += c;
-      before += i < b ? c : 0;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      before += __shfl_xor_sync(0xffffffffu, before, o);
-      all += __shfl_xor_sync(0xffffffffu, all, o);
-    }
-    if ((threadIdx.x & 31) == 0) {
-      wsum[0][threadIdx.x >> 5] = before;
-      wsum[1][threadIdx.x >> 5] = all;
-    }
-    __syncthreads();
-    pb0 = 0;
-    ptot = 0;
-#pragma unroll
-    for (int w = 0; w < kCombineThreads / 32; ++w) {
-      pb0 += wsum[0][w];
-      ptot += wsum[1][w];
-    }
-    int64_t ctx = p.context_lens[b];
-    ctx = ctx > cap ? cap : ctx;
-    nsub = ctx > 0 ? static_cast<int>((ctx + kSub - 1) / kSub) : 0;
-  }
-  if (nsub <= 0) return;
-  const int W = p.W;
-  const int64_t total = (int64_t)ptot * p.SPS;
-  const int64_t sstart = (int64_t)pb0 * p.SPS + (int64_t)segx * nsub, send = sstart + nsub;
-  const int g0 = static_cast<int>(((sstart + 1) * W - 1) / total);
-  const int g1 = static_cast<int>((send * W - 1) / total);
-  if (g0 == g1) return;  // finished inside one slice
-  const int nrec = g1 - g0 + 1;
-  grid_dep_wait();  // the main kernel's records are complete and visible
-  const int kvh = segx / p.HT, ht = segx - kvh * p.HT;
-  const int h0 = kvh * p.group + ht * 16, hn = min(16, p.group - ht * 16);
-  const bool g0_first = (int64_t)g0 * total / W == sstart;
   const int tid = threadIdx.x;
-  auto rec = [&](int r) -> int64_t {  // record row base (h = 0), or -1 for an empty slice
-    const int gg = g0 + r;
-    if ((int64_t)gg * total / W == (int64_t)(gg + 1) * total / W) return -1;
-    const int sl = (r == 0 && !g0_first) ? 1 : 0;
-    return (int64_t)(gg * 2 + sl) * 16;
-  };
-  // One pass: thread (item, stripe) merges the records stripe, stripe +
-  // stripes, ... of one (row, 8 columns) item online (running max in the
-  // log2 domain, rescaled l and O), four records' loads in flight at a
-  // time; then the stripes of each item are merged by log-sum-exp through
-  // shared memory.  One dependent round of global loads per four records.
-  const int items = hn * (D / 8);
-  const int stripes = kCombineThreads / items;
-  const int item = tid % items, stripe = tid / items;
+  const int sid = blockIdx.x;
+  const int b = sid / p.SPS, segx = sid - b * p.SPS;
+  const int64_t cap = p.bt_width * (int64_t)p.bs;
+  int before = 0, all = 0;
+  for (int i = tid; i < p.B; i += kCombineThreads) {
+    int64_t ctx = p.context_lens[i];
+    ctx = ctx > cap ? cap : ctx;
+    const int cnt = ctx > 0 ? static_cast<int>((ctx + kSub - 1) / kSub) : 0;
+    all += cnt;
+    before += i < b ? cnt : 0;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    before += __shfl_xor_sync(0xffffffffu, before, o);
+    all += __shfl_xor_sync(0xffffffffu, all, o);
+  }
+  if ((tid & 31) == 0) {
+    wsum[0][tid >> 5] = before;
+    wsum[1][tid >> 5] = all;
+  }
+  __syncthreads();
+  before = all = 0;
+#pragma unroll
+  for (int w = 0; w < kCombineThreads / 32; ++w) {
+    before += wsum[0][w];
+    all += wsum[1][w];
+  }
+  int64_t ctx = p.context_lens[b];
+  ctx = ctx > cap ? cap : ctx;
+  const int nsub = ctx > 0 ? static_cast<int>((ctx + kSub - 1) / kSub) : 0;
+  if (nsub == 0) return;
+  const int64_t total = (int64_t)all * p.SPS;
+  const int G = static_cast<int>(total < (int64_t)p.grid ? total : (int64_t)p.grid);
+  const int64_t start = (int64_t)before * p.SPS + (int64_t)segx * nsub, end = start + nsub;
+  auto cta_of = [&](int64_t xx) { return static_cast<int>(((xx + 1) * G - 1) / total); };
+  const int c0 = cta_of(start), c1 = cta_of(end - 1);
+  if (c0 == c1) return;  // finished inside one CTA of the main kernel
+  int kvh0, h0, hn;
+  seg_heads<PK>(p, segx, kvh0, h0, hn);
+  const int item = tid % kItems, stripe = tid / kItems;
+  const int r = blockIdx.y * kCombineRows + item / (D / 8), d = 8 * (item % (D / 8));
+  const int hh = row_head<PK>(r, p.group, hn);
+  grid_dep_wait();  // the main kernel's records are complete and visible
+  grid_dep_launch();
   float mrun = -INFINITY, lrun = 0.f;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (stripe < stripes) {
-    const int h = item / (D / 8), d = 8 * (item - h * (D / 8));
-    for (int r0 = stripe; r0 < nrec; r0 += 4 * stripes) {
-      float2 ml[4];
-      float4 v0[4], v1[4];
+  if (hh >= 0) {
+    for (int cb = c0 + stripe; cb <= c1; cb += 8 * kStripes) {  // eight records' loads in flight
+      float2 ml[8];
+      float4 v0[8], v1[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int r = r0 + u * stripes;
-        const int64_t base = r < nrec ? rec(r) : -1;
+      for (int u = 0; u < 8; ++u) {
+        const int cc = cb + u * kStripes;
         ml[u] = make_float2(-INFINITY, 0.f);
         v0[u] = v1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (base >= 0) {
-          ml[u] = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (base + h) * 2));
-          const float4* src = reinterpret_cast<const float4*>(p.part_o + (base + h) * D + d);
-          v0[u] = __ldcg(src);
-          v1[u] = __ldcg(src + 1);
+        if (cc <= c1) {
+          const int sl = start < (int64_t)cc * total / G ? 0 : 1;
+          const float* rec = p.part + (((int64_t)cc * 2 + sl) * 16 + r) * kRec;
+          ml[u] = __ldcg(reinterpret_cast<const float2*>(rec));
+          v0[u] = __ldcg(reinterpret_cast<const float4*>(rec + 4 + d));
+          v1[u] = __ldcg(reinterpret_cast<const float4*>(rec + 8 + d));
         }
       }
+      float mx = mrun;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (ml[u].x == -INFINITY) continue;
-        const float mnew = fmaxf(mrun, ml[u].x);
-        const float a = exp2f(mrun - mnew), wt = exp2f(ml[u].x - mnew);  // a = 0 on the first record
-        lrun = lrun * a + ml[u].y * wt;
-        acc[0] = fmaf(wt, v0[u].x, acc[0] * a);
-        acc[1] = fmaf(wt, v0[u].y, acc[1] * a);
-        acc[2] = fmaf(wt, v0[u].z, acc[2] * a);
-        acc[3] = fmaf(wt, v0[u].w, acc[3] * a);
-        acc[4] = fmaf(wt, v1[u].x, acc[4] * a);
-        acc[5] = fmaf(wt, v1[u].y, acc[5] * a);
-        acc[6] = fmaf(wt, v1[u].z, acc[6] * a);
-        acc[7] = fmaf(wt, v1[u].w, acc[7] * a);
-        mrun = mnew;
+      for (int u = 0; u < 8; ++u) mx = fmaxf(mx, ml[u].x);
+      if (mx == -INFINITY) continue;
+      const float a = exp2f(mrun - mx);  // 0 on the first batch
+      lrun *= a;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] *= a;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wt = exp2f(ml[u].x - mx);  // 0 for absent records
+        lrun = fmaf(wt, ml[u].y, lrun);
+        axpy8(wt, v0[u], v1[u], acc);
       }
+      mrun = mx;
     }
   }
-  sm_m[tid] = mrun;
-  sm_l[tid] = lrun;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) red[tid * 8 + e] = acc[e];
-  __syncthreads();
-  if (tid < items) {
-    const int h = tid / (D / 8), d = 8 * (tid - h * (D / 8));
+  if (kStripes > 1) {
+    sm_m[tid] = mrun;
+    sm_l[tid] = lrun;
+    sm_acc[tid][0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    sm_acc[tid][1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    __syncthreads();
+    if (stripe != 0 || hh < 0) return;
     float mx = -INFINITY;
-    for (int s2 = 0; s2 < stripes; ++s2) mx = fmaxf(mx, sm_m[s2 * items + tid]);
-    float lt = 0.f, sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s2 = 0; s2 < stripes; ++s2) {
-      const int t2 = s2 * items + tid;
-      const float ms = sm_m[t2];
-      if (ms == -INFINITY) continue;
-      const float wt = exp2f(ms - mx);
-      lt = fmaf(sm_l[t2], wt, lt);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sum[e] = fmaf(red[t2 * 8 + e], wt, sum[e]);
+    for (int s2 = 0; s2 < kStripes; ++s2) mx = fmaxf(mx, sm_m[s2 * kItems + item]);
+    lrun = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < kStripes; ++s2) {
+      const int t2 = s2 * kItems + item;
+      const float wt = exp2f(sm_m[t2] - mx);
+      lrun = fmaf(wt, sm_l[t2], lrun);
+      axpy8(wt, sm_acc[t2][0], sm_acc[t2][1], acc);
     }
-    T* out = reinterpret_cast<T*>(p.out);
-    store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d, sum, 1.f / lt);
+  }
+  if (hh < 0) return;
+  T* out = reinterpret_cast<T*>(p.out);
+  store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d, acc, 1.f / lrun);
+}
+
+// Merge `nw` warp records (m, l, O) of row h, column d (log2 domain).
+template <int D>
+__device__ __forceinline__ void merge_records(const float* area, int nw, int h, int d, float& m, float& l,
+                                              float& acc) {
+  constexpr int kRec = D + 4;
+  m = -INFINITY;
+  for (int w = 0; w < nw; ++w) m = fmaxf(m, area[(w * 16 + h) * kRec]);
+  l = 0.f;
+  acc = 0.f;
+  for (int w = 0; w < nw; ++w) {
+    const float* r = area + (w * 16 + h) * kRec;
+    if (r[0] == -INFINITY) continue;  // warp saw no token of this piece
+    const float sc = exp2f(r[0] - m);
+    l += sc * r[1];
+    acc += sc * r[4 + d];
   }
 }
 
@@ -763,20 +930,21 @@ __global__ void __launch_bounds__(NW * 32) decode_split_kernel(const __grid_cons
   if (lane == 0) {
     for (int j = 0; j < STAGES && j < nj; ++j) issue(j);
   }
-  WarpState<T, D> ws;
+  using WS = WarpState<T, D, 1>;
+  WS ws;
   ws.reset();
-  ws.load_q(reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_s0, p.q_s1, h0, hn, lane);
+  WS::load_q(ws.qa, reinterpret_cast<const T*>(p.q) + (int64_t)b * p.q_s0, p.q_s1, h0, p.group, hn, lane);
   bool ok = true;
   for (int j = 0; j < nj; ++j) {
     const int stage = j % STAGES;
     if (ok) ok = mbar_wait(&wbar[stage], (j / STAGES) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
     const uint32_t kbase = smem_u32(ring + stage * C::kStageBytes);
     const int valid = static_cast<int>(min((int64_t)kSub, ctx - (int64_t)(s0 + warp + j * NW) * kSub));
-    const uint32_t vbase = kbase + C::kColTiles * kTileBytes;
-    ws.template consume<1>(&kbase, &vbase, &valid, p.scale_log2, lane);
+    ws.template consume<1>(&kbase, &valid, p.scale_log2, lane);
     __syncwarp();
     if (lane == 0 && j + STAGES < nj) issue(j + STAGES);
   }
+  ws.reduce_l();
   ws.store(merge + warp * 16 * (D + 4), lane);
   __syncthreads();
 
@@ -827,24 +995,22 @@ int current_device() {
   return dev;
 }
 
-// Kernel shapes: (warps per CTA, ring stages per warp).
-// Two CTAs per SM (about 107 KB of shared memory each), so a CTA's start-up
-// and merge tail overlap the other CTA's streaming — and, with PDL, the next
-// kernel's CTAs.
-#ifndef PA_FLAT_NW64
-#define PA_FLAT_NW64 4
-#endif
-#ifndef PA_FLAT_ST64
-#define PA_FLAT_ST64 4
-#endif
-constexpr int kFlatNW64 = PA_FLAT_NW64, kFlatST64 = PA_FLAT_ST64;
-constexpr int kFlatNW128 = 2, kFlatST128 = 4;
-#ifndef PA_FLAT_CTAS
-#define PA_FLAT_CTAS 2
-#endif
-constexpr int kFlatCtasPerSm = PA_FLAT_CTAS;
-constexpr int flat_nw(int D) { return D == 64 ? kFlatNW64 : kFlatNW128; }
+// Shapes of the balanced kernel: warps per CTA, ring stages per warp and
+// sub-blocks per consume step, per (head_dim, KV heads per warp).  Two CTAs
+// per SM (~87 KB of shared memory each at D = 64), so one CTA's start-up and
+// merge tail overlap the other's streaming and, with PDL, the next kernel's
+// CTAs move in as soon as one exits.  A stage is one sub-block of every head
+// of the pack: 8 KB (D = 64, PK = 2) to 16 KB (D = 128, PK = 2).
+template <int D, int PK> struct FlatShape;
+template <> struct FlatShape<64, 2> { static constexpr int NW = 4, ST = 2, NSUB = 1; };
+template <> struct FlatShape<64, 1> { static constexpr int NW = 4, ST = 4, NSUB = 2; };
+template <> struct FlatShape<128, 2> { static constexpr int NW = 2, ST = 2, NSUB = 1; };
+template <> struct FlatShape<128, 1> { static constexpr int NW = 2, ST = 4, NSUB = 2; };
+constexpr int kFlatCtasPerSm = 2;
 constexpr int kSplitNW = 4, kSplitST = 4;
+
+// Two KV heads per warp when a GQA group fits half the MMA rows.
+bool flat_pack2(int hq, int hkv) { return hkv % 2 == 0 && hq / hkv <= 8; }
 
 template <typename K>
 bool set_smem_attr(K kern, size_t bytes, bool* done) {
@@ -858,15 +1024,17 @@ bool set_smem_attr(K kern, size_t bytes, bool* done) {
   return true;
 }
 
-template <typename T, int D, int NW, int ST, int CTAS>
+template <typename T, int D, int PK>
 int launch_flat(const FlatParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int grid, cudaStream_t st) {
-  using C = FlatCfg<D, NW, ST>;
-  auto kern = decode_flat_kernel<T, D, NW, ST, CTAS>;
+  using S = FlatShape<D, PK>;
+  using C = FlatCfg<D, PK, S::NW, S::ST>;
+  auto kern = decode_flat_kernel<T, D, PK, S::NW, S::ST, S::NSUB, kFlatCtasPerSm>;
   static bool done[64] = {};
   if (!set_smem_attr(kern, C::kSmem, done)) return PA_ERR_CUDA;
-  const int r = launch_pdl(kern, dim3(grid), dim3(NW * 32), C::kSmem, st, tk, tv, p);
+  const int r = launch_pdl(kern, dim3(grid), dim3(S::NW * 32), C::kSmem, st, tk, tv, p);
   if (r != PA_OK) return r;
-  return launch_pdl(decode_combine_kernel<T, D>, dim3(p.B * p.SPS), dim3(kCombineThreads), 0, st, p);
+  return launch_pdl(decode_combine_kernel<T, D, PK>, dim3(p.B * p.SPS, 16 / kCombineRows), dim3(kCombineThreads), 0,
+                    st, p);
 }
 
 template <typename T, int D>
@@ -897,15 +1065,22 @@ bool fast_path_ok(int dtype, int D, int bs, int64_t num_blocks, const void* q, i
   return true;
 }
 
-// Which kernel a call uses and how many partials it may write.
+// Which kernel a call uses and how much workspace it needs.
 struct DecodePlan {
   enum Kind { kFlat, kSplit, kGeneric } kind;
-  int grid;         // flat: CTAs
-  int split_sub;    // split: sub-blocks per partition
-  int split_tokens; // generic: tokens per partition
-  int splits;       // split / generic: partitions per sequence (max)
+  int grid;          // flat: CTAs
+  int split_sub;     // split: sub-blocks per partition
+  int split_tokens;  // generic: tokens per partition
+  int splits;        // split / generic: partitions per sequence (max)
   size_t ws_bytes;
 };
+
+// Workspace of the balanced kernel: status word, the ticket range of the
+// other decode kernels (unused here, kept so one zeroing rule serves every
+// path), then two partial records of 16 rows x (D + 4) floats per CTA.
+size_t flat_ws_bytes(int batch, int hq, int D, int grid) {
+  return 256 + align256(sizeof(int) * (size_t)batch * hq) + align256((size_t)grid * 2 * 16 * (D + 4) * sizeof(float));
+}
 
 DecodePlan plan_decode(int batch, int hkv, int hq, int D, int bs, int64_t bt_width, int partition_tokens,
                        int dtype) {
@@ -913,25 +1088,19 @@ DecodePlan plan_decode(int batch, int hkv, int hq, int D, int bs, int64_t bt_wid
   const int group = hq / hkv;
   const int sms = num_sms(current_device());
   const int64_t max_tok = bt_width * bs;
-  const size_t tickets = align256(sizeof(int) * (size_t)batch * hq);
-  if (tc_shape_ok(dtype, D, bs) && partition_tokens == 0 && batch <= kFlatMaxBatch) {
+  if (tc_shape_ok(dtype, D, bs) && batch <= kFlatMaxBatch) {
+    // Explicit partitions (partition_tokens > 0) take the balanced kernel as
+    // well: its pieces are LSE-merged exactly like partitions, only cut where
+    // the load balance puts them.
     pl.kind = DecodePlan::kFlat;
     pl.grid = sms * kFlatCtasPerSm;
-    const size_t W = (size_t)pl.grid * flat_nw(D);
-    const size_t ml = align256(sizeof(float) * 2 * 16 * 2 * W);
-    const size_t po = align256(sizeof(float) * 2 * 16 * (size_t)D * W);
-    pl.ws_bytes = 256 + tickets + ml + po;
+    pl.ws_bytes = flat_ws_bytes(batch, hq, D, pl.grid);
     return pl;
   }
   if (tc_shape_ok(dtype, D, bs)) {
     pl.kind = DecodePlan::kSplit;
     const int64_t max_sub = (max_tok + kSub - 1) / kSub;
-    int64_t split;
-    if (partition_tokens > 0) {
-      split = (partition_tokens + kSub - 1) / kSub;
-    } else {  // batch too large for the flat kernel's prefix table
-      split = max_sub;
-    }
+    int64_t split = partition_tokens > 0 ? (partition_tokens + kSub - 1) / kSub : max_sub;
     split = split > max_sub ? max_sub : (split < 1 ? 1 : split);
     pl.split_sub = static_cast<int>(split);
     pl.splits = static_cast<int>((max_sub + split - 1) / split);
@@ -983,7 +1152,8 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
                 int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
                 int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
                 int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
-                void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused);
+                void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused,
+                int flags = 0);
 
 }  // namespace
 }  // namespace pa
@@ -1029,6 +1199,37 @@ extern "C" int pa_paged_decode_write(const void* q, int64_t q_s0, int64_t q_s1, 
                          dtype, 0, workspace, workspace_bytes, stream);
 }
 
+extern "C" int pa_paged_decode_ex(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k, const void* new_v,
+                                  const int64_t* slot_mapping, void* k_pool_layer, void* v_pool_layer,
+                                  int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                                  const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
+                                  const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
+                                  int num_q_heads, float scale, int dtype, int partition_tokens, int flags,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace pa;
+  if (batch < 0 || (flags & ~PA_DECODE_EARLY_INPUTS)) return PA_ERR_INVALID;
+  if (batch == 0) return PA_OK;
+  const bool write = new_k != nullptr || new_v != nullptr || slot_mapping != nullptr;
+  if (!write)
+    return decode_impl(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads, head_dim,
+                       block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch, num_q_heads, scale,
+                       dtype, partition_tokens, workspace, workspace_bytes, stream, nullptr, nullptr, flags);
+  if (new_k == nullptr || new_v == nullptr || slot_mapping == nullptr || partition_tokens != 0) return PA_ERR_INVALID;
+  if (!((reinterpret_cast<uintptr_t>(new_k) | reinterpret_cast<uintptr_t>(new_v)) & 15)) {
+    FusedWrite fw{new_k, new_v, slot_mapping};
+    bool fused = false;
+    const int r = decode_impl(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads,
+                              head_dim, block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch,
+                              num_q_heads, scale, dtype, 0, workspace, workspace_bytes, stream, &fw, &fused, flags);
+    if (r != PA_OK || fused) return r;
+  }
+  // Not fusable here: the scatter, then decode; the decode then reads pool
+  // rows the scatter just wrote, so it waits before its first read.
+  return pa_paged_decode_write(q, q_s0, q_s1, new_k, new_v, slot_mapping, k_pool_layer, v_pool_layer, num_blocks,
+                               block_size, num_kv_heads, head_dim, block_tables, bt_stride, bt_width, context_lens, out,
+                               o_s0, o_s1, batch, num_q_heads, scale, dtype, workspace, workspace_bytes, stream);
+}
+
 namespace pa {
 namespace {
 
@@ -1036,9 +1237,10 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
                 int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
                 int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
                 int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
-                void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused) {
+                void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused,
+                int flags) {
   if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0 ||
-      block_size <= 0 || num_blocks <= 0 || bt_width <= 0 || partition_tokens < 0)
+      block_size <= 0 || num_blocks <= 0 || bt_width <= 0 || partition_tokens < 0 || (flags & ~PA_DECODE_EARLY_INPUTS))
     return PA_ERR_INVALID;
   if (batch == 0) return PA_OK;
   if (q == nullptr || k_pool_layer == nullptr || v_pool_layer == nullptr || block_tables == nullptr ||
@@ -1060,26 +1262,26 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
     pl.split_tokens = static_cast<int>((max_tok + chunk - 1) / chunk * chunk);
     pl.splits = 1;
   }
+  if (fw != nullptr && pl.kind != DecodePlan::kFlat) {
+    if (fused != nullptr) *fused = false;  // only the balanced kernel fuses the write
+    return PA_OK;
+  }
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   if (ws == nullptr || workspace_bytes < pl.ws_bytes || (reinterpret_cast<uintptr_t>(ws) & 255))
     return PA_ERR_WORKSPACE;
   int* status = reinterpret_cast<int*>(ws);
-  const size_t off_ml = 256 + align256(sizeof(int) * (size_t)batch * num_q_heads);
 
   if (pl.kind == DecodePlan::kFlat || pl.kind == DecodePlan::kSplit) {
     CUtensorMap tk, tv;
     const uint64_t slots = static_cast<uint64_t>(num_blocks) * block_size;
     const uint64_t s1b = static_cast<uint64_t>(head_dim) * 2;
     const uint64_t s2b = s1b * num_kv_heads;
-#ifndef PA_DECODE_L2_PROMOTION
-#define PA_DECODE_L2_PROMOTION CU_TENSOR_MAP_L2_PROMOTION_L2_128B
-#endif
     // Rows of one KV head are 128 B with a Hkv*128 B stride; a wider L2
     // promotion would drag the other heads' rows in ahead of their readers.
     if (make_map_3d(&tk, dtype, k_pool_layer, head_dim, num_kv_heads, slots, s1b, s2b, 64, 1, 16,
-                    CU_TENSOR_MAP_SWIZZLE_128B, PA_DECODE_L2_PROMOTION) != PA_OK ||
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B) != PA_OK ||
         make_map_3d(&tv, dtype, v_pool_layer, head_dim, num_kv_heads, slots, s1b, s2b, 64, 1, 16,
-                    CU_TENSOR_MAP_SWIZZLE_128B, PA_DECODE_L2_PROMOTION) != PA_OK)
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B) != PA_OK)
       return PA_ERR_CUDA;
     const float scale_log2 = scale * 1.4426950408889634f;
     if (pl.kind == DecodePlan::kFlat) {
@@ -1098,15 +1300,14 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
       p.Hq = num_q_heads;
       p.Hkv = num_kv_heads;
       p.group = group;
-      p.HT = (group + 15) / 16;
-      p.SPS = num_kv_heads * p.HT;
+      const bool pk2 = flat_pack2(num_q_heads, num_kv_heads);
+      p.HT = pk2 ? 1 : (group + 15) / 16;
+      p.SPS = pk2 ? num_kv_heads / 2 : num_kv_heads * p.HT;
       p.bs = block_size;
       p.scale_log2 = scale_log2;
-      p.W = pl.grid * flat_nw(head_dim);
-      const size_t ml_bytes = align256(sizeof(float) * 2 * 16 * 2 * (size_t)p.W);
-      const size_t po_bytes = align256(sizeof(float) * 2 * 16 * (size_t)head_dim * p.W);
-      p.part_ml = reinterpret_cast<float*>(ws + off_ml);
-      p.part_o = reinterpret_cast<float*>(ws + off_ml + ml_bytes);
+      p.grid = pl.grid;
+      p.early = (flags & PA_DECODE_EARLY_INPUTS) ? 1 : 0;
+      p.part = reinterpret_cast<float*>(ws + 256 + align256(sizeof(int) * (size_t)batch * num_q_heads));
       p.status = status;
       p.new_k = fw ? fw->new_k : nullptr;
       p.new_v = fw ? fw->new_v : nullptr;
@@ -1115,12 +1316,16 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
       p.v_pool = const_cast<void*>(v_pool_layer);
       p.num_slots = static_cast<int64_t>(num_blocks) * block_size;
       if (fused != nullptr) *fused = fw != nullptr;
-      constexpr int CT = kFlatCtasPerSm;
-      if (dtype == PA_DTYPE_BF16)
-        return head_dim == 64 ? launch_flat<__nv_bfloat16, 64, kFlatNW64, kFlatST64, CT>(p, tk, tv, pl.grid, st)
-                              : launch_flat<__nv_bfloat16, 128, kFlatNW128, kFlatST128, CT>(p, tk, tv, pl.grid, st);
-      return head_dim == 64 ? launch_flat<__half, 64, kFlatNW64, kFlatST64, CT>(p, tk, tv, pl.grid, st)
-                            : launch_flat<__half, 128, kFlatNW128, kFlatST128, CT>(p, tk, tv, pl.grid, st);
+      const int g = pl.grid;
+      if (dtype == PA_DTYPE_BF16) {
+        using B16 = __nv_bfloat16;
+        if (head_dim == 64)
+          return pk2 ? launch_flat<B16, 64, 2>(p, tk, tv, g, st) : launch_flat<B16, 64, 1>(p, tk, tv, g, st);
+        return pk2 ? launch_flat<B16, 128, 2>(p, tk, tv, g, st) : launch_flat<B16, 128, 1>(p, tk, tv, g, st);
+      }
+      if (head_dim == 64)
+        return pk2 ? launch_flat<__half, 64, 2>(p, tk, tv, g, st) : launch_flat<__half, 64, 1>(p, tk, tv, g, st);
+      return pk2 ? launch_flat<__half, 128, 2>(p, tk, tv, g, st) : launch_flat<__half, 128, 1>(p, tk, tv, g, st);
     }
     if (pl.splits > 65535) return PA_ERR_INVALID;
     const WorkspaceLayout wl = workspace_layout(batch, num_q_heads, head_dim, pl.splits);

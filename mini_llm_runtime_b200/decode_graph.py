@@ -68,6 +68,7 @@ class PagedDecodeGraph:
         scale: float | None = None,
         write_kv: bool = True,
         fuse_write: bool = True,
+        early_inputs: bool = True,
     ):
         dev = _lib.require_cuda(cache.k_cache, what="PagedDecodeGraph")
         if cache.dtype not in (torch.float16, torch.bfloat16, torch.float32):
@@ -85,6 +86,11 @@ class PagedDecodeGraph:
         # The KV write rides in the decode kernel (pa_paged_decode_write)
         # unless the split-KV path is asked for.
         self.fuse_write = fuse_write and partition_tokens == 0
+        # Inside the graph a layer's decode follows the previous layer's
+        # decode (or the input copy), which writes no metadata and no pool
+        # row of this layer: its kernel may start on them before that one
+        # ends (PA_DECODE_EARLY_INPUTS).
+        self._flags = _lib.PA_DECODE_EARLY_INPUTS if early_inputs else 0
         self.scale = (1.0 / math.sqrt(cache.head_dim)) if scale is None else float(scale)
         L, B, H, D, HKV = len(self.layers), batch, num_q_heads, cache.head_dim, cache.num_kv_heads
         dt = cache.dtype
@@ -181,27 +187,24 @@ class PagedDecodeGraph:
             nk, nv, q, o = self.new_k[i], self.new_v[i], self.q[i], self.out[i]
             kp, vp = c.k_cache[layer], c.v_cache[layer]
             write = self.write_kv and not warm
-            if write and self.fuse_write:
-                st = lib.pa_paged_decode_write(
-                    q.data_ptr(), q.stride(0), q.stride(1), nk.data_ptr(), nv.data_ptr(), self.slot_mapping.data_ptr(),
-                    kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D, self.block_tables.data_ptr(),
-                    self.block_tables.stride(0), self.width, self.context_lens.data_ptr(), o.data_ptr(), o.stride(0),
-                    o.stride(1), B, H, self.scale, self._code, self.workspace.data_ptr(), self.workspace.numel(),
-                    stream)
-                _lib.check(st, "pa_paged_decode_write")
-            else:
-                if write:
-                    st = lib.pa_kv_scatter(
-                        nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0),
-                        nv.stride(1), nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(),
-                        vp.data_ptr(), num_slots, HKV, D, self._code, stream)
-                    _lib.check(st, "pa_kv_scatter")
-                st = lib.pa_paged_decode(
-                    q.data_ptr(), q.stride(0), q.stride(1), kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D,
-                    self.block_tables.data_ptr(), self.block_tables.stride(0), self.width, self.context_lens.data_ptr(),
-                    o.data_ptr(), o.stride(0), o.stride(1), B, H, self.scale, self._code, self.partition_tokens,
-                    self.workspace.data_ptr(), self.workspace.numel(), stream)
-                _lib.check(st, "pa_paged_decode")
+            fused = write and self.fuse_write
+            if write and not fused:
+                st = lib.pa_kv_scatter(
+                    nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0),
+                    nv.stride(1), nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(),
+                    vp.data_ptr(), num_slots, HKV, D, self._code, stream)
+                _lib.check(st, "pa_kv_scatter")
+            # After a separate scatter the decode reads pool rows that kernel
+            # just wrote, so it waits before touching anything.
+            flags = self._flags if (fused or not write) else 0
+            st = lib.pa_paged_decode_ex(
+                q.data_ptr(), q.stride(0), q.stride(1), nk.data_ptr() if fused else None,
+                nv.data_ptr() if fused else None, self.slot_mapping.data_ptr() if fused else None,
+                kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D, self.block_tables.data_ptr(),
+                self.block_tables.stride(0), self.width, self.context_lens.data_ptr(), o.data_ptr(), o.stride(0),
+                o.stride(1), B, H, self.scale, self._code, 0 if fused else self.partition_tokens, flags,
+                self.workspace.data_ptr(), self.workspace.numel(), stream)
+            _lib.check(st, "pa_paged_decode_ex")
             if io and i in last_of_chunk:
                 a = last_of_chunk[i]
                 done = torch.cuda.Event()
@@ -258,7 +261,7 @@ class PagedDecodeGraph:
         and, when the write is not fused into it, the KV scatter."""
         c = self.cache
         balanced = (c.dtype in (torch.bfloat16, torch.float16) and c.head_dim in (64, 128) and c.block_size % 16 == 0
-                    and c.block_size <= 256 and self.partition_tokens == 0 and self.batch <= 1024)
+                    and c.block_size <= 256 and self.batch <= 1024)
         per_layer = 2 if balanced else 1
         if self.write_kv and not (self.fuse_write and balanced):
             per_layer += 1

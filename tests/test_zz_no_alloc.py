@@ -61,11 +61,11 @@ def test_noalloc_rejects_requests_beyond_its_scratch(cuda_device):
     """A request whose scratch exceeds the fixed array fails with
     PA_ERR_CAPACITY before anything is launched."""
     lib = _lib.load()
-    # 1024 sequences x 256 query heads x 64 partitions needs far more than 16 MiB.
-    need = lib.pa_decode_workspace_bytes(1024, 8, 256, 128, 16, 4096, 1024, 2)
+    # 4096 sequences x 256 query heads x 64 partitions needs far more than 16 MiB.
+    need = lib.pa_decode_workspace_bytes(4096, 8, 256, 128, 16, 4096, 1024, 2)
     assert need > 16 << 20
     dummy = torch.zeros(16, dtype=torch.int64, device=cuda_device)
     p = dummy.data_ptr()
-    st = lib.pa_paged_decode_noalloc(p, 0, 0, p, p, 1, 16, 8, 128, p, 0, 4096, p, p, 0, 0, 1024, 256, 1.0, 2, 1024,
+    st = lib.pa_paged_decode_noalloc(p, 0, 0, p, p, 1, 16, 8, 128, p, 0, 4096, p, p, 0, 0, 4096, 256, 1.0, 2, 1024,
                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert st == _lib.PA_ERR_CAPACITY
