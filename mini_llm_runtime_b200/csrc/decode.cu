@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBars);
   __shared__ int warp_sums[NW];
   __shared__ int ent_seg[2 * NW];  // segment id of warp w's cut first (2w) / last (2w+1) piece, or -1
-  __shared__ int run_first[2 * NW], run_last[2 * NW], run_sid[2 * NW];
+  __shared__ int run_sid[2 * NW], run_nrec[2 * NW], run_rec[2 * NW][2 * NW];  // records: float offsets into smem
   __shared__ int nruns_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -649,26 +649,24 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
       const int sid = ent_seg[f];
       if (sid < 0) continue;
       if (sid != prev) {
-        run_first[n] = f;
         run_sid[n] = sid;
+        run_nrec[n] = 0;
         ++n;
         prev = sid;
       }
-      run_last[n - 1] = f;
+      // Entry f's record: a warp's ring (last piece) or its staging slot.
+      run_rec[n - 1][run_nrec[n - 1]++] = (f & 1) ? (f >> 1) * STAGES * C::kStageBytes / 4
+                                                  : (C::kOffStaging + (f >> 1) * C::kRecBytes) / 4;
     }
     nruns_s = n;
   }
   __syncthreads();
-  auto rec_row = [&](int f, int r) -> const float* {  // entry f's record, row r
-    return ((f & 1) ? reinterpret_cast<const float*>(smem + (f >> 1) * STAGES * C::kStageBytes)
-                    : staging + (f >> 1) * 16 * kRec) +
-           r * kRec;
-  };
+  const float* smem_f = reinterpret_cast<const float*>(smem);
   constexpr int kItems = 16 * (D / 8);  // (row, 8 columns)
   const int nruns = nruns_s;
   for (int w = tid; w < nruns * kItems; w += NT) {
     const int ri = w / kItems, it = w - ri * kItems;
-    const int sid = run_sid[ri], f0 = run_first[ri], f1 = run_last[ri];
+    const int sid = run_sid[ri], nrec = run_nrec[ri];
     const int r = it / (D / 8), d = 8 * (it - r * (D / 8));
     const Seg S = seg_by_id(pre, p.SPS, sid);
     int kvh0, h0, hn;
@@ -678,13 +676,15 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
     // Two passes (the maximum, then independent weighted sums) keep the
     // records' contributions free of a serial rescale chain.
     float mx = -INFINITY;
-    for (int f = f0; f <= f1; ++f)
-      if (ent_seg[f] == sid) mx = fmaxf(mx, rec_row(f, r)[0]);
+#pragma unroll
+    for (int k = 0; k < 2 * NW; ++k)
+      if (k < nrec) mx = fmaxf(mx, smem_f[run_rec[ri][k] + r * kRec]);
     float l = 0.f;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int f = f0; f <= f1; ++f) {
-      if (ent_seg[f] != sid) continue;
-      const float* rec = rec_row(f, r);
+#pragma unroll
+    for (int k = 0; k < 2 * NW; ++k) {
+      if (k >= nrec) break;
+      const float* rec = smem_f + run_rec[ri][k] + r * kRec;
       const float wt = exp2f(rec[0] - mx);
       l = fmaf(wt, rec[1], l);
       axpy8(wt, *reinterpret_cast<const float4*>(rec + 4 + d), *reinterpret_cast<const float4*>(rec + 8 + d), acc);
@@ -706,7 +706,11 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
 // return at once.  Launched with PDL right behind the main kernel: the
 // segment's bounds come from the context lengths (an input the main kernel
 // does not write) before the wait, so only the record loads remain after it.
-constexpr int kCombineThreads = 128;
+// Its CTAs are small (64 threads, ~7 K registers) so all of them fit beside
+// the main kernel's CTAs, and each lets the next kernel launch as soon as it
+// starts: that kernel's CTAs then take each SM the main kernel frees and run
+// their own start-up while this merge is still pending.
+constexpr int kCombineThreads = 64;
 constexpr int kCombineRows = 4;
 
 template <typename T, int D, int PK>
@@ -722,6 +726,7 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
   const int sid = blockIdx.x;
   const int b = sid / p.SPS, segx = sid - b * p.SPS;
   const int64_t cap = p.bt_width * (int64_t)p.bs;
+  grid_dep_launch();
   int before = 0, all = 0;
   for (int i = tid; i < p.B; i += kCombineThreads) {
     int64_t ctx = p.context_lens[i];
@@ -762,7 +767,6 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
   const int r = blockIdx.y * kCombineRows + item / (D / 8), d = 8 * (item % (D / 8));
   const int hh = row_head<PK>(r, p.group, hn);
   grid_dep_wait();  // the main kernel's records are complete and visible
-  grid_dep_launch();
   float mrun = -INFINITY, lrun = 0.f;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (hh >= 0) {
