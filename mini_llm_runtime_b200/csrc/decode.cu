@@ -706,16 +706,18 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
 // return at once.  Launched with PDL right behind the main kernel: the
 // segment's bounds come from the context lengths (an input the main kernel
 // does not write) before the wait, so only the record loads remain after it.
-// Its CTAs are small (64 threads, ~7 K registers) so all of them fit beside
+// Its CTAs are small (64 threads, at most 128 registers) so they fit beside
 // the main kernel's CTAs, and each lets the next kernel launch as soon as it
 // starts: that kernel's CTAs then take each SM the main kernel frees and run
-// their own start-up while this merge is still pending.
+// their own start-up while this merge is still pending.  A CTA covers ROWS
+// rows; when segments span many CTAs (long sequences) ROWS shrinks so the
+// records of one item are split over several threads (stripes).
 constexpr int kCombineThreads = 64;
-constexpr int kCombineRows = 4;
 
-template <typename T, int D, int PK>
-__global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatParams p) {
+template <typename T, int D, int PK, int ROWS>
+__global__ void __launch_bounds__(kCombineThreads, 8) decode_combine_kernel(FlatParams p) {
   constexpr int kRec = D + 4;
+  constexpr int kCombineRows = ROWS;
   constexpr int kItems = kCombineRows * (D / 8);  // (row, 8 columns) per CTA
   constexpr int kStripes = kCombineThreads / kItems;
   static_assert(kStripes >= 1 && kCombineThreads % kItems == 0, "combine layout");
@@ -779,7 +781,9 @@ __global__ void __launch_bounds__(kCombineThreads) decode_combine_kernel(FlatPar
         ml[u] = make_float2(-INFINITY, 0.f);
         v0[u] = v1[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (cc <= c1) {
-          const int sl = start < (int64_t)cc * total / G ? 0 : 1;
+          // The segment starts inside CTA c0's range (slot 1 there) and
+          // before the range of every later CTA (slot 0).
+          const int sl = cc == c0 ? 1 : 0;
           const float* rec = p.part + (((int64_t)cc * 2 + sl) * 16 + r) * kRec;
           ml[u] = __ldcg(reinterpret_cast<const float2*>(rec));
           v0[u] = __ldcg(reinterpret_cast<const float4*>(rec + 4 + d));
@@ -1037,8 +1041,13 @@ int launch_flat(const FlatParams& p, const CUtensorMap& tk, const CUtensorMap& t
   if (!set_smem_attr(kern, C::kSmem, done)) return PA_ERR_CUDA;
   const int r = launch_pdl(kern, dim3(grid), dim3(S::NW * 32), C::kSmem, st, tk, tv, p);
   if (r != PA_OK) return r;
-  return launch_pdl(decode_combine_kernel<T, D, PK>, dim3(p.B * p.SPS, 16 / kCombineRows), dim3(kCombineThreads), 0,
-                    st, p);
+  // One item per thread (ROWS = 512 / D) unless segments span more than eight
+  // CTAs on average; then one row per CTA and the records go over stripes.
+  constexpr int kRowsWide = kCombineThreads * 8 / D;
+  if ((int64_t)grid > 8 * (int64_t)p.B * p.SPS)
+    return launch_pdl(decode_combine_kernel<T, D, PK, 1>, dim3(p.B * p.SPS, 16), dim3(kCombineThreads), 0, st, p);
+  return launch_pdl(decode_combine_kernel<T, D, PK, kRowsWide>, dim3(p.B * p.SPS, 16 / kRowsWide),
+                    dim3(kCombineThreads), 0, st, p);
 }
 
 template <typename T, int D>
