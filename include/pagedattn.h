@@ -216,6 +216,25 @@ PA_API int pa_paged_decode_noalloc(const void* q, int64_t q_s0, int64_t q_s1, co
                                    int num_q_heads, float scale, int dtype, int partition_tokens, void* stream);
 
 /*
+ * Copies the status word of pa_paged_decode_noalloc's built-in scratch to
+ * *status_out (host memory) in `stream` order: 0, or PA_DEVICE_TIMEOUT_* when
+ * a bounded wait of the last call on this device gave up (its output is then
+ * garbage).  Read *status_out after synchronising `stream`.  Allocates
+ * nothing; no counterpart in the reference (its decode has no device waits).
+ */
+PA_API int pa_decode_noalloc_status(int* status_out, void* stream);
+
+/*
+ * Self-test of the device-side failure path (no counterpart in the
+ * reference): launches one bounded wait on an mbarrier that nothing arrives
+ * on.  After limit_ns (1 us .. 2 s) of %globaltimer the wait gives up, writes
+ * PA_DEVICE_TIMEOUT_TMA into *status (device int, left alone if already
+ * non-zero) and the kernel returns — the same path every kernel here takes
+ * when a TMA copy or tensor-core step never completes.  No fault, no hang.
+ */
+PA_API int pa_selftest_wait_timeout(int* status, int64_t limit_ns, void* stream);
+
+/*
  * Causal chunk-prefill over a paged cache, batched over sequences.
  *
  * Sequence s owns packed query rows [cu_q_lens[s], cu_q_lens[s+1]) of q; its

@@ -14,14 +14,18 @@ from .paged_attention import (
     paged_attention_prefill_varlen,
     paged_decode_with_kv_write,
 )
+from ._lib import PagedAttentionError, check_device_status, device_status, reset_device_status
 from .decode_graph import PagedDecodeGraph
 from .paged_kv_cache import PagedKVCache
 from .qwen2_attention import Qwen2Attention
 
 __all__ = [
+    "PagedAttentionError",
     "PagedDecodeGraph",
     "PagedKVCache",
     "Qwen2Attention",
+    "check_device_status",
+    "device_status",
     "paged_attention_accumulator_cuda",
     "paged_attention_decode",
     "paged_attention_decode_batch_parallel",
@@ -29,4 +33,5 @@ __all__ = [
     "paged_attention_prefill_chunk_tiled",
     "paged_attention_prefill_varlen",
     "paged_decode_with_kv_write",
+    "reset_device_status",
 ]

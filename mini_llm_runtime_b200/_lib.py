@@ -8,6 +8,7 @@ for any op in this package.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -22,6 +23,8 @@ PA_ERR_CUDA = -3
 PA_ERR_WORKSPACE = -4
 PA_ERR_CAPACITY = -5
 PA_DECODE_EARLY_INPUTS = 1
+PA_DEVICE_TIMEOUT_TMA = 101
+PA_DEVICE_TIMEOUT_MMA = 102
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
 
@@ -69,6 +72,8 @@ SIGNATURES: dict[str, tuple] = {
          _i32, _i32, _i32, _c_void_p, _i64, _i64, _i32, _i64, _i32, _i32, _f32, _i32, _c_void_p, _c_void_p],
     ),
     "pa_accumulate_pv": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "pa_decode_noalloc_status": (_i32, [_c_void_p, _c_void_p]),
+    "pa_selftest_wait_timeout": (_i32, [_c_void_p, _i64, _c_void_p]),
 }
 
 _lib = None
@@ -143,7 +148,12 @@ def dtype_code(dtype: torch.dtype) -> int:
 # re-zeroed first.  Calls on one stream are ordered, so they never overlap.
 # ---------------------------------------------------------------------------
 _workspaces: dict[tuple[int, int], "_Workspace"] = {}
-_status_words: dict[int, torch.Tensor] = {}
+_control_blocks: dict[tuple[int, int], torch.Tensor] = {}
+
+# With MINI_LLM_RUNTIME_B200_SYNC_CHECK=1 every op synchronises after its
+# launch and raises on a device-side status (a debugging aid: it costs a host
+# round trip per op).
+SYNC_CHECK = os.environ.get("MINI_LLM_RUNTIME_B200_SYNC_CHECK", "0") not in ("", "0")
 
 
 class _Workspace:
@@ -159,17 +169,70 @@ def _align256(x: int) -> int:
 PREFILL_CONTROL_INTS = 4  # PA_PREFILL_CONTROL_INTS
 
 
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
 def status_word(device: torch.device) -> torch.Tensor:
-    """Per-device control block of pa_chunk_prefill (int32[4], zeroed once):
-    [0] is the status the kernels set when a bounded wait gives up, [1..2]
-    the self-rewinding work-claim counters.  Calls that use it are ordered on
-    the current stream."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    t = _status_words.get(idx)
+    """Control block of pa_chunk_prefill for the current stream of `device`
+    (int32[4], zeroed once): [0] is the status the kernels set when a
+    bounded wait gives up, [1..2] the self-rewinding work-claim counters.
+    One block per (device, stream), so calls that share it are ordered on
+    that stream and calls on different streams never share counters."""
+    key = (_dev_index(device), stream_handle(device))
+    t = _control_blocks.get(key)
     if t is None:
         t = torch.zeros(PREFILL_CONTROL_INTS, dtype=torch.int32, device=device)
-        _status_words[idx] = t
+        _control_blocks[key] = t
     return t
+
+
+def device_status(device: torch.device | None = None) -> list[tuple[str, int]]:
+    """(what, code) for every non-zero device status word this package owns on
+    `device` (all devices when None): the decode workspaces' status words and
+    the prefill control blocks.  Synchronises the device (one D2H read)."""
+    words = []
+    for (idx, st), ws in _workspaces.items():
+        if device is None or idx == _dev_index(device):
+            words.append((f"decode workspace (device {idx}, stream {st:#x})", ws.tensor[:4].view(torch.int32)[:1]))
+    for (idx, st), cb in _control_blocks.items():
+        if device is None or idx == _dev_index(device):
+            words.append((f"prefill control block (device {idx}, stream {st:#x})", cb[:1]))
+    if not words:
+        return []
+    codes = torch.cat([w.to("cpu", non_blocking=False) for _, w in words]).tolist()
+    return [(what, c) for (what, _), c in zip(words, codes) if c != 0]
+
+
+def reset_device_status(device: torch.device | None = None) -> None:
+    """Re-zero every status word, ticket and work counter this package owns
+    on `device` (all devices when None): after a device-side timeout those
+    may hold values a normal call never leaves behind."""
+    for (idx, _), ws in _workspaces.items():
+        if device is None or idx == _dev_index(device):
+            ws.tensor.zero_()
+            ws.clean_end = ws.tensor.numel()
+    for (idx, _), cb in _control_blocks.items():
+        if device is None or idx == _dev_index(device):
+            cb.zero_()
+
+
+def check_device_status(device: torch.device | None = None) -> None:
+    """Raise PagedAttentionError if a kernel of this package recorded a
+    device-side failure (a bounded wait that gave up; its outputs are then
+    garbage).  The words are re-zeroed before raising, so the next call starts
+    clean.  Synchronises the device."""
+    bad = device_status(device)
+    if bad:
+        reset_device_status(device)
+        msg = "; ".join(f"{what}: {load().pa_status_string(code).decode()} (status {code})" for what, code in bad)
+        raise PagedAttentionError(f"device-side failure: {msg}")
+
+
+def after_launch(device: torch.device) -> None:
+    """Debug hook run after every launch (MINI_LLM_RUNTIME_B200_SYNC_CHECK)."""
+    if SYNC_CHECK:
+        check_device_status(device)
 
 
 def prepare_workspace(ws: "_Workspace", batch: int, num_q_heads: int) -> None:

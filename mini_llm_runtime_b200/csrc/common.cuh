@@ -114,13 +114,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Returns false (and records `code`) when the phase did not complete within
-// kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// limit_ns (kWaitLimitNs unless a self-test asks for less).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+    if ((i & 63) == 0 && globaltimer_ns() - t0 > limit_ns) break;
   }
   record_status(status, code);
   return false;

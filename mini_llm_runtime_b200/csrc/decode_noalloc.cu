@@ -68,3 +68,18 @@ extern "C" int pa_paged_decode_noalloc(const void* q, int64_t q_s0, int64_t q_s1
                          block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch, num_q_heads, scale,
                          dtype, partition_tokens, scratch, kNoAllocScratchBytes, stream);
 }
+
+// The status word of the built-in scratch (0, or PA_DEVICE_TIMEOUT_* when a
+// bounded wait of the last pa_paged_decode_noalloc call on this device gave
+// up), copied to host memory in stream order.  Allocates nothing.
+extern "C" int pa_decode_noalloc_status(int* status_out, void* stream) {
+  using namespace pa;
+  if (status_out == nullptr) return PA_ERR_INVALID;
+  void* scratch = nullptr;
+  const int r = scratch_address(&scratch);
+  if (r != PA_OK) return r;
+  if (cudaMemcpyAsync(status_out, scratch, sizeof(int), cudaMemcpyDeviceToHost,
+                      reinterpret_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return PA_ERR_CUDA;
+  return PA_OK;
+}

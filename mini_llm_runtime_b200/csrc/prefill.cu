@@ -3,8 +3,9 @@
 // Replaces paged_attention_prefill_chunk_tiled / _tiled_reference
 // (kernels/reference/paged_attention.py:282-434), batched over sequences
 // with varlen metadata (cu_q_lens = ModelBatch.query_start_loc,
-// runtime/model_runner.py:14-27).  BF16/F16 with head_dim 64 and block sizes
-// that tile 128 tokens go to the tcgen05 kernel in prefill_tc.cu; everything
+// runtime/model_runner.py:14-27).  BF16/F16 with head_dim 64 or 128 and block
+// sizes that are a multiple of 16 go to the tcgen05 kernel in prefill_tc.cu
+// (when the pointers and strides suit its TMA maps); everything
 // else (F32 — the CUDA-core path the parity contract asks for — and odd
 // shapes) runs the CUDA-core kernel in attn_generic.cu, one query row per
 // CTA with context = prefix + i + 1.

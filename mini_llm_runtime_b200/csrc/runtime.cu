@@ -47,7 +47,27 @@ int num_sms(int device) {
   return cached[device];
 }
 
+// One bounded wait on an mbarrier that nothing ever arrives on: the wait runs
+// out after limit_ns and records PA_DEVICE_TIMEOUT_TMA in *status, the path
+// every kernel takes when a copy or tensor-core step never completes.
+__global__ void wait_timeout_selftest_kernel(int* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    mbar_wait(&bar, 0, status, PA_DEVICE_TIMEOUT_TMA, limit_ns);
+  }
+}
+
 }  // namespace pa
+
+extern "C" int pa_selftest_wait_timeout(int* status, int64_t limit_ns, void* stream) {
+  if (status == nullptr || limit_ns < 1000 || limit_ns > 2000000000LL) return PA_ERR_INVALID;
+  pa::wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      status, static_cast<uint64_t>(limit_ns));
+  PA_CHECK_LAUNCH();
+  return PA_OK;
+}
 
 extern "C" const char* pa_status_string(int status) {
   switch (status) {
@@ -63,4 +83,4 @@ extern "C" const char* pa_status_string(int status) {
   }
 }
 
-extern "C" int pa_abi_version(void) { return 1; }
+extern "C" int pa_abi_version(void) { return 2; }

@@ -18,6 +18,12 @@ Typical use::
     g.run()                      # validate metadata on the host, replay
     g.synchronize(); out = g.host_output   # [layers, B, Hq, D]
 
+``host_inputs`` is read by copies inside the replay, after ``run()`` has
+returned: refill it for the next step only after ``synchronize()`` or
+``wait_inputs_consumed()``, or the replay in flight may copy a mix of two
+steps.  ``synchronize()`` also raises ``PagedAttentionError`` when a kernel of
+the step recorded a device-side failure (a bounded wait that gave up).
+
 The metadata checks are the ones Qwen2Attention.forward_decode_batch_with_cache
 runs before touching the cache (model/qwen2.py:553-602), done on the pinned
 host copies, so a step never needs a device->host sync.
@@ -127,6 +133,7 @@ class PagedDecodeGraph:
         # Private, zeroed once; every replay leaves the tickets at zero.
         self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
         self.graph = None
+        self._replayed = None  # event after the last replay (its copies included)
         self._stream = torch.cuda.Stream(dev)
         self._h2d = torch.cuda.Stream(dev)
         self._d2h = torch.cuda.Stream(dev)
@@ -249,10 +256,27 @@ class PagedDecodeGraph:
         self._stream.wait_stream(cur)
         with torch.cuda.stream(self._stream):
             self.graph.replay()
+            self._replayed = torch.cuda.Event()
+            self._replayed.record(self._stream)
         cur.wait_stream(self._stream)
 
+    def wait_inputs_consumed(self) -> None:
+        """Block the host until the last replay has copied ``host_inputs`` to
+        the device (it waits for the whole replay), so the next step's inputs
+        can be written."""
+        if self._replayed is not None:
+            self._replayed.synchronize()
+
     def synchronize(self) -> None:
+        """Wait for the step, then raise ``PagedAttentionError`` if one of its
+        kernels recorded a device-side failure in the step's workspace (the
+        workspace is re-zeroed first, so later steps start clean)."""
         torch.cuda.current_stream(self.device).synchronize()
+        code = int(self.workspace[:4].view(torch.int32)[0].item())
+        if code != 0:
+            self.workspace.zero_()
+            msg = self._lib.pa_status_string(code).decode()
+            raise _lib.PagedAttentionError(f"PagedDecodeGraph step: {msg} (status {code})")
 
     @property
     def launches_per_step(self) -> int:

@@ -93,6 +93,7 @@ def _decode_launch(
             int(partition_tokens), ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
         )
     _lib.check(st, "pa_paged_decode")
+    _lib.after_launch(dev)
     return out
 
 
@@ -163,6 +164,7 @@ def paged_decode_with_kv_write(
             ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
         )
     _lib.check(st, "pa_paged_decode_write")
+    _lib.after_launch(dev)
     return out
 
 
@@ -324,6 +326,7 @@ def _prefill_launch(
             float(scale), _lib.dtype_code(q.dtype), _lib.status_word(dev).data_ptr(), _lib.stream_handle(dev),
         )
     _lib.check(st, "pa_chunk_prefill")
+    _lib.after_launch(dev)
     return out
 
 

@@ -30,6 +30,7 @@ The .npz files are committed; this script is how they were made.
 from __future__ import annotations
 
 import argparse
+import os
 import math
 import sys
 from pathlib import Path
@@ -294,8 +295,11 @@ def gen_accumulator():
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-src", default="/root/reference/src")
+    ap.add_argument("--ref-src", default=os.environ.get("MINI_LLM_RUNTIME_SRC"),
+                    help="src/ directory of a mini-llm-runtime checkout (or set MINI_LLM_RUNTIME_SRC)")
     args = ap.parse_args()
+    if not args.ref_src:
+        ap.error("--ref-src (or MINI_LLM_RUNTIME_SRC) is required")
     sys.path.insert(0, args.ref_src)
     from mini_llm_runtime.kernels.reference import paged_attention as pa_ref
     from mini_llm_runtime.runtime.paged_kv_cache import PagedKVCache
