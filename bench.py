@@ -23,9 +23,14 @@ the step's inputs copied from pinned host memory and the outputs copied back
 inside the timed region; ``roofline`` for the decode kernel; ``cpu_baseline``
 = the oracle port on the host cores (rank 0, N=1).
 
+``e2e_per_layer`` = the same metric through the per-layer drop-in call
+(24 x paged_decode_with_kv_write per step, each layer's inputs copied from
+pinned host memory and its output copied back).
+
 ``--impl reference`` times the reference's algorithm on the host CPU (the
 oracle port; the reference is PyTorch code with no compiled path to build) on
-a bounded sample of the same workload: one layer of the batch per step.
+the same workload: the rank-0 batch of the same metadata draw, 24 layers
+(KV write + decode) per step, all host cores.
 """
 
 from __future__ import annotations
@@ -363,44 +368,64 @@ def run_kernel_case(args):
 # ---------------------------------------------------------------------------
 
 
-def cpu_reference_sample(steps: int, warmup: int, seed: int = 0):
+def bench_config(world: int, rank0_batch: int) -> dict:
+    """The workload both arms report (the driver compares the two)."""
+    return {
+        "workload": "config2: bf16 batched paged decode (KV write + decode per layer), 24 layers, "
+                    "14/2 heads, D64, bs16, global batch 64*N sharded by request (LPT on ctx), "
+                    "ctx U[128,4096], pool = blocks*1.1 per rank",
+        "global_batch": BATCH * world,
+        "parallelism": f"request-sharded dp{world}, no communication",
+        "rank0_batch": rank0_batch,
+        "l2": "inputs larger than L2 (1.66 GB of KV streamed per step per GPU), no flush",
+    }
+
+
+def cpu_reference_sample(steps: int, warmup: int, layers: int, world: int = 1, rank: int = 0):
     """Time the oracle port of paged_attention_decode_batch_parallel plus the
-    write_slots restatement on one layer of the workload per step."""
+    write_slots restatement (paged_kv_cache.py:194-249) on the host cores:
+    `layers` layers of the GPU arm's rank-0 batch (the same metadata draw) per
+    step.  The layers share one FP32 pool (the CPU work per layer does not
+    depend on the values)."""
     from oracle import paged_attention_oracle as O
 
-    ctx, tables, slots, nb = make_metadata(seed)
-    rng = np.random.default_rng(seed + 1)
+    ctx, tables, slots, nb = make_metadata(1000, world, rank)
+    n = len(ctx)
+    rng = np.random.default_rng(1001)
     k = rng.standard_normal((1, nb, BS, HKV, D), dtype=np.float32)
     v = rng.standard_normal((1, nb, BS, HKV, D), dtype=np.float32)
-    q = O.round_to_bf16(rng.standard_normal((BATCH, HQ, D), dtype=np.float32))
-    nk = O.round_to_bf16(rng.standard_normal((BATCH, HKV, D), dtype=np.float32))
-    nv = O.round_to_bf16(rng.standard_normal((BATCH, HKV, D), dtype=np.float32))
+    q = O.round_to_bf16(rng.standard_normal((n, HQ, D), dtype=np.float32))
+    nk = O.round_to_bf16(rng.standard_normal((n, HKV, D), dtype=np.float32))
+    nv = O.round_to_bf16(rng.standard_normal((n, HKV, D), dtype=np.float32))
     threads = os.cpu_count() or 1
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
-        O.write_slots(k, v, slots, nk, nv, 0)
-        O.decode_batch_threaded(q, k[0], v[0], tables, ctx, BS, threads)
+        for _ in range(layers):
+            O.write_slots(k, v, slots, nk, nv, 0)
+            O.decode_batch_threaded(q, k[0], v[0], tables, ctx, BS, threads)
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
-    per_layer = statistics.median(times)
-    gbs = algorithmic_bytes(ctx)["kv"] / per_layer / 1e9
+    step = statistics.median(times)
+    kv = algorithmic_bytes(ctx)["kv"] * layers
     return {
-        "value": gbs,
+        "value": kv / step / 1e9,
         "unit": UNIT,
         "cores": threads,
         "kind": "port",
-        "sample": f"one layer of the config-2 batch (64 seqs, sum ctx {int(ctx.sum())}) per step, "
-                  f"median of {steps} steps, FP32 math on BF16-valued inputs",
-        "ms_per_layer": per_layer * 1e3,
+        "sample": f"{layers} layer(s) of the rank-0 batch ({n} seqs, sum ctx {int(ctx.sum())}) per step, "
+                  f"median of {steps} steps, FP32 numpy on BF16-valued inputs, {threads} threads",
+        "ms_per_step": step * 1e3,
+        "spread": {"min_gbs": kv / max(times) / 1e9, "max_gbs": kv / min(times) / 1e9, "steps": steps},
+        "batch": n,
     }
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return
-    r = cpu_reference_sample(args.steps, args.warmup)
+    r = cpu_reference_sample(args.steps, args.warmup, LAYERS, world, 0)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -409,15 +434,14 @@ def run_reference(args, rank, world):
         "n_gpus": args.gpus,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": r["ms_per_layer"],
+        "ms_per_step": r["ms_per_step"],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": "config2: bf16 batched paged decode, 24 layers, 14/2 heads, D64, bs16, "
-                               "batch 64, ctx U[128,4096] (one layer per step on the CPU)"},
-        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "config": bench_config(world, r["batch"]),
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "spread")},
         "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -457,6 +481,42 @@ def stage(graph, inputs: dict, device_resident: bool) -> None:
             graph._dev_inputs[k].copy_(v)
         else:
             graph.host_inputs[k].copy_(v)
+
+
+def run_per_layer_e2e(w: dict, device, steps: int, warmup: int, barrier) -> dict:
+    """Time `steps` decode steps through the per-layer drop-in call
+    (paged_decode_with_kv_write) with host I/O per layer; CUDA events on the
+    current stream."""
+    from mini_llm_runtime_b200 import paged_decode_with_kv_write
+
+    cache, hin = w["cache"], w["inputs"]
+    pin = {k: v.pin_memory() for k, v in hin.items()}
+    dev = {k: torch.empty_like(v, device=device) for k, v in hin.items()}
+    n = len(w["ctx"])
+    out_h = torch.empty(LAYERS, n, HQ, D, dtype=torch.bfloat16).pin_memory()
+
+    def step():
+        for k in ("slot_mapping", "block_tables", "context_lens"):
+            dev[k].copy_(pin[k], non_blocking=True)
+        for layer in range(LAYERS):
+            for k in ("q", "new_k", "new_v"):
+                dev[k][layer].copy_(pin[k][layer], non_blocking=True)
+            o = paged_decode_with_kv_write(dev["q"][layer], dev["new_k"][layer], dev["new_v"][layer],
+                                           dev["slot_mapping"], cache.k_cache[layer], cache.v_cache[layer],
+                                           dev["block_tables"], dev["context_lens"], BS)
+            out_h[layer].copy_(o, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    barrier()
+    h2d = sum(t.numel() * t.element_size() for t in pin.values())
+    return {"ms": e0.elapsed_time(e1) / steps, "h2d": h2d, "d2h": out_h.numel() * out_h.element_size()}
 
 
 def main():
@@ -556,6 +616,14 @@ def main():
     barrier()
     e2e_ms = reduce(e0.elapsed_time(e1) / args.steps, dist.ReduceOp.MAX if world > 1 else None)
 
+    # ---- end to end per layer: the drop-in call, one layer at a time --------
+    # Each layer copies its own q / new_k / new_v from pinned host memory,
+    # calls paged_decode_with_kv_write (the fused write_slots + batched decode
+    # of Qwen2Attention.forward_decode_batch_with_cache) and copies its output
+    # back, all on the current stream; the metadata goes over once per step.
+    e2l = run_per_layer_e2e(w, device, args.steps, warmup, barrier)
+    e2l_ms = reduce(e2l["ms"], dist.ReduceOp.MAX if world > 1 else None)
+
     total_kv = reduce(nbytes["kv"] * LAYERS, dist.ReduceOp.SUM if world > 1 else None)
     tokens = reduce(batch, dist.ReduceOp.SUM if world > 1 else None)
     value = total_kv / (ms_step * 1e-3) / 1e9
@@ -580,8 +648,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_reference_sample(steps=5, warmup=1)
-        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        r = cpu_reference_sample(steps=20, warmup=2, layers=1)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "spread")}
 
     if rank == 0:
         line = {
@@ -597,21 +665,19 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {
-                "workload": "config2: bf16 batched paged decode (KV write + decode per layer), 24 layers, "
-                            "14/2 heads, D64, bs16, global batch 64*N sharded by request (LPT on ctx), "
-                            "ctx U[128,4096], pool = blocks*1.1 per rank",
-                "global_batch": BATCH * world,
-                "parallelism": f"request-sharded dp{world}, no communication",
-                "rank0_batch": batch,
-                "l2": "inputs larger than L2 (1.66 GB of KV streamed per step per GPU), no flush",
-                "launch": "one CUDA graph per step (48 kernel nodes)",
-            },
+            "config": bench_config(world, batch),
+            "launch": "one CUDA graph per step: 24 x (decode with the fused KV write + combine), "
+                      "PA_DECODE_EARLY_INPUTS",
             "tok_per_s": tokens / (ms_step * 1e-3),
             "frac_of_hbm_peak": value / world / peak,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms, "tok_per_s": tokens / (e2e_ms * 1e-3),
                     "path": "PagedDecodeGraph.run(): host metadata checks, pinned H2D, 24x(KV write+decode), D2H"},
+            "e2e_per_layer": {"value": total_kv / (e2l_ms * 1e-3) / 1e9, "unit": UNIT,
+                              "h2d_bytes_per_step": e2l["h2d"], "d2h_bytes_per_step": e2l["d2h"],
+                              "ms_per_step": e2l_ms,
+                              "path": "24 x paged_decode_with_kv_write, each with its layer's pinned H2D of "
+                                      "q/new_k/new_v and D2H of its output"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
                          "kernel": "decode_flat_kernel<bf16,64>",
