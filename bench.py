@@ -71,6 +71,8 @@ def parse_args():
                     help="time one kernel case alone (secondary configs; the small ncu targets)")
     ap.add_argument("--layers", type=int, default=None, help="layers the --kernel case rotates over")
     ap.add_argument("--reps", type=int, default=None, help="graph replays timed by the --kernel case")
+    ap.add_argument("--mode", choices=["request-shard", "head-shard"], default="request-shard",
+                    help="head-shard: config 3 split by KV head over the GPUs, NCCL all-gather of head outputs")
     return ap.parse_args()
 
 
@@ -519,6 +521,86 @@ def run_per_layer_e2e(w: dict, device, steps: int, warmup: int, barrier) -> dict
     return {"ms": e0.elapsed_time(e1) / steps, "h2d": h2d, "d2h": out_h.numel() * out_h.element_size()}
 
 
+def run_head_shard(args, rank, world, local_rank):
+    """Config 3 (8 x 32,768 tokens, 14/2 heads) decoded with its KV heads split
+    over the ranks: each rank streams its heads' KV from its own pools and one
+    NCCL all-gather per layer rebuilds [B, Hq, D].  Layers x (decode +
+    all-gather) are captured in one CUDA graph; `value` is the whole batch's
+    algorithmic KV bytes per second (max over ranks)."""
+    import torch.distributed as dist
+
+    from mini_llm_runtime_b200 import _lib
+    from mini_llm_runtime_b200.head_shard import HeadShardedDecode, head_slices
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29531")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=device)
+    _lib.load()
+    layers = 4
+    ctx = np.full(8, 32768, dtype=np.int64)
+    q_sl, kv_sl = head_slices(HQ, HKV, world, rank)
+    hq_l, hkv_l = q_sl.stop - q_sl.start, kv_sl.stop - kv_sl.start
+    rng = np.random.default_rng(13)
+    tables, nb = _random_tables(rng, ctx, BS)
+    gen = torch.Generator(device=device).manual_seed(13 + rank)
+    k = _bf16_randn((layers, nb, BS, hkv_l, D), device, gen)
+    v = _bf16_randn((layers, nb, BS, hkv_l, D), device, gen)
+    q = _bf16_randn((layers, len(ctx), hq_l, D), device, gen)
+    bt, cl = torch.tensor(tables, device=device), torch.tensor(ctx, device=device)
+    hs = HeadShardedDecode(HQ, HKV)
+    out = torch.empty(layers, len(ctx), HQ, D, dtype=torch.bfloat16, device=device)
+    part = torch.empty(layers, world, len(ctx), hq_l, D, dtype=torch.bfloat16, device=device)
+
+    def body(gather_only=False):
+        for l in range(layers):
+            if gather_only:
+                dist.all_gather_into_tensor(part[l], q[l].contiguous())
+            else:
+                hs(q[l], k[l], v[l], bt, cl, BS, out=out[l])
+
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        body()
+        body(True)
+    torch.cuda.synchronize()
+    graphs = {}
+    for name, only in (("step", False), ("gather", True)):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            body(only)
+        graphs[name] = g
+    times = {}
+    for name, g in graphs.items():
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / (args.steps * layers)], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times[name] = float(t.item())
+    kv = int(ctx.sum()) * HKV * D * 2 * 2
+    if rank == 0:
+        print(json.dumps({
+            "mode": "head-shard", "metric": METRIC, "value": kv / (times["step"] * 1e-3) / 1e9, "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic", "ms_per_layer": times["step"], "allgather_ms_per_layer": times["gather"],
+            "config": {"workload": "config3: 8 x 32768 tokens, 14/2 heads, D64, bs16, KV heads split over the "
+                                   "GPUs, NCCL all-gather of the [B, Hq/N, D] head outputs per layer",
+                       "layers_in_graph": layers}}), flush=True)
+    del graphs
+    dist.barrier(device_ids=[local_rank])
+    dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     rank, world, local_rank = env_rank()
@@ -527,6 +609,9 @@ def main():
         return
     if args.kernel:
         run_kernel_case(args)
+        return
+    if args.mode == "head-shard":
+        run_head_shard(args, rank, world, local_rank)
         return
 
     import torch.distributed as dist

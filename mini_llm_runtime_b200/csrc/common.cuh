@@ -152,7 +152,7 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, i
   return false;
 }
 
-// 3-D tiled TMA load, no multicast: box lands densely in shared memory and
+// 3-D tiled TMA load into this CTA: the box lands densely in shared memory and
 // completes `bar`'s transaction count.
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                             int c1, int c2) {
