@@ -566,27 +566,29 @@ def run_head_shard(args, rank, world, local_rank):
         body()
         body(True)
     torch.cuda.synchronize()
-    graphs = {}
-    for name, only in (("step", False), ("gather", True)):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=s):
-            body(only)
-        graphs[name] = g
-    times = {}
-    for name, g in graphs.items():
+    def time_graph(gather_only: bool) -> float:
+        # The graph holds NCCL calls: it must be gone before the process
+        # group is destroyed, so it lives only inside this function.
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            body(gather_only)
         for _ in range(max(args.warmup, 3)):
-            g.replay()
+            graph.replay()
         dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            g.replay()
+            graph.replay()
         e1.record()
         torch.cuda.synchronize()
+        del graph
         t = torch.tensor([e0.elapsed_time(e1) / (args.steps * layers)], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        times[name] = float(t.item())
+        return float(t.item())
+
+    times = {"step": time_graph(False), "gather": time_graph(True)}
+    torch.cuda.synchronize()
     kv = int(ctx.sum()) * HKV * D * 2 * 2
     if rank == 0:
         print(json.dumps({
@@ -596,7 +598,6 @@ def run_head_shard(args, rank, world, local_rank):
             "config": {"workload": "config3: 8 x 32768 tokens, 14/2 heads, D64, bs16, KV heads split over the "
                                    "GPUs, NCCL all-gather of the [B, Hq/N, D] head outputs per layer",
                        "layers_in_graph": layers}}), flush=True)
-    del graphs
     dist.barrier(device_ids=[local_rank])
     dist.destroy_process_group()
 
