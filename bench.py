@@ -228,10 +228,14 @@ def _bf16_randn(shape, device, gen):
     return torch.randn(shape, device=device, generator=gen).to(torch.bfloat16)
 
 
-def _decode_case(device, layers, ctx, hq, hkv, d, partition, seed):
+FP8_SCALES = (0.0625, 0.0625)  # k_scale, v_scale of the FP8 cases (N(0,1) values, well inside +-448 * scale)
+
+
+def _decode_case(device, layers, ctx, hq, hkv, d, partition, seed, fp8=False):
     """A decode kernel case: ``fn(l)`` runs layer l; ``inputs`` holds the
     tensors (the parity tests run the oracle on them); ``work`` is the
-    algorithmic bytes of one launch."""
+    algorithmic bytes of one launch.  ``fp8``: the pools hold the e4m3
+    quantization of the same N(0, 1) draw (clamp(x / scale) to nearest even)."""
     from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel, paged_attention_decode_split_kv
 
     rng = np.random.default_rng(seed)
@@ -240,14 +244,21 @@ def _decode_case(device, layers, ctx, hq, hkv, d, partition, seed):
     k = _bf16_randn((layers, nb, BS, hkv, d), device, gen)
     v = _bf16_randn((layers, nb, BS, hkv, d), device, gen)
     q = _bf16_randn((layers, len(ctx), hq, d), device, gen)
+    ks, vs = FP8_SCALES if fp8 else (1.0, 1.0)
+    if fp8:
+        k = (k.float() / ks).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
+        v = (v.float() / vs).clamp_(-448.0, 448.0).to(torch.float8_e4m3fn)
     bt, cl = torch.tensor(tables, device=device), torch.tensor(ctx, device=device)
+    sc = {"k_scale": ks, "v_scale": vs}
     if partition:
-        fn = lambda l: paged_attention_decode_split_kv(q[l], k[l], v[l], bt, cl, BS, partition)  # noqa: E731
+        fn = lambda l: paged_attention_decode_split_kv(q[l], k[l], v[l], bt, cl, BS, partition, **sc)  # noqa: E731
     else:
-        fn = lambda l: paged_attention_decode_batch_parallel(q[l], k[l], v[l], bt, cl, BS)  # noqa: E731
-    work = int(ctx.sum()) * hkv * d * 2 * 2 + 2 * len(ctx) * hq * d * 2 + int(((ctx + BS - 1) // BS).sum()) * 8
+        fn = lambda l: paged_attention_decode_batch_parallel(q[l], k[l], v[l], bt, cl, BS, **sc)  # noqa: E731
+    esize = 1 if fp8 else 2
+    work = (int(ctx.sum()) * hkv * d * esize * 2 + 2 * len(ctx) * hq * d * 2
+            + int(((ctx + BS - 1) // BS).sum()) * 8)
     inputs = {"kind": "decode", "q": q, "k": k, "v": v, "tables": tables, "ctx": ctx, "block_tables": bt,
-              "context_lens": cl, "partition": partition}
+              "context_lens": cl, "partition": partition, "k_scale": ks, "v_scale": vs}
     return {"fn": fn, "work": work, "inputs": inputs}
 
 
@@ -282,6 +293,11 @@ def _case_config2(device, layers):
     return _decode_case(device, layers, ctx, HQ, HKV, D, 0, 11)
 
 
+def _case_config2_fp8(device, layers):
+    ctx = make_metadata(1000)[0]
+    return _decode_case(device, layers, ctx, HQ, HKV, D, 0, 11, fp8=True)
+
+
 def _case_config3(device, layers):
     ctx = np.full(8, 32768, dtype=np.int64)
     return _decode_case(device, layers, ctx, HQ, HKV, D, 32768 // 16, 13)
@@ -307,6 +323,9 @@ def _case_config5_prefill(device, layers):
 KERNEL_CASES = {
     "decode-config2": (_case_config2, "hbm", 8,
                        "config2 one layer: bf16 batched decode, B64, 14/2, D64, ctx U[128,4096]"),
+    "decode-config2-fp8": (_case_config2_fp8, "hbm", 8,
+                           "config2 one layer over an FP8 (e4m3) KV pool: bf16 queries, B64, 14/2, D64, "
+                           "ctx U[128,4096]; bytes counted at 1 B per KV element"),
     "split-config3": (_case_config3, "hbm", 4,
                       "config3: bf16 split-KV decode, B8 x 32768, 14/2, D64, 16 partitions of 2048"),
     "prefill-config4": (_case_config4, "tensor", 4,
@@ -727,7 +746,7 @@ def main():
     # ---- secondary configs, one kernel at a time (same GPU, after the step) --
     secondary = {}
     if world == 1:
-        for name in ("split-config3", "prefill-config4", "decode-config5", "prefill-config5"):
+        for name in ("split-config3", "prefill-config4", "decode-config5", "prefill-config5", "decode-config2-fp8"):
             r = time_kernel_case(name, device)
             secondary[name] = {k: r[k] for k in ("workload", "us_per_launch", "achieved", "unit", "frac")}
             torch.cuda.empty_cache()

@@ -53,6 +53,7 @@ extern "C" {
 #define PA_DTYPE_F16 1
 #define PA_DTYPE_BF16 2
 #define PA_DTYPE_F64 3
+#define PA_DTYPE_FP8_E4M3 4 /* KV pools only (torch.float8_e4m3fn), with a scale per pool */
 
 /* Flags of pa_paged_decode_ex. */
 #define PA_DECODE_EARLY_INPUTS 1 /* metadata and pools may be read before the PDL wait */
@@ -86,6 +87,44 @@ PA_API int pa_kv_scatter(const void* k, int64_t k_s0, int64_t k_s1, int64_t k_s2
                   int64_t v_s1, int64_t v_s2, int src_dtype, const void* slot_mapping, int slot_is_int64,
                   int64_t num_tokens, void* k_pool_layer, void* v_pool_layer, int64_t num_slots,
                   int num_kv_heads, int head_dim, int pool_dtype, void* stream);
+
+/*
+ * FP8 KV-cache pools (PA_DTYPE_FP8_E4M3, torch.float8_e4m3fn) — a storage
+ * format of the reference's PagedKVCache (runtime/paged_kv_cache.py:25-35)
+ * that halves the bytes decode streams; the reference has no FP8 pool, so
+ * these entry points extend its write_slots / decode / prefill contracts
+ * with one scale per pool (k_scale, v_scale > 0, finite): a stored element
+ * is clamp(x / scale, -448, 448) rounded to nearest even (the division in
+ * FP32), and attention reads it back as element * scale.
+ *
+ * pa_kv_scatter_fp8: pa_kv_scatter into FP8 pools (any source dtype and
+ * strides; slots outside the pool skipped).  Replaces
+ * PagedKVCache.write_slots (runtime/paged_kv_cache.py:194-249) for FP8 pools.
+ */
+PA_API int pa_kv_scatter_fp8(const void* k, int64_t k_s0, int64_t k_s1, int64_t k_s2, const void* v, int64_t v_s0,
+                             int64_t v_s1, int64_t v_s2, int src_dtype, const void* slot_mapping, int slot_is_int64,
+                             int64_t num_tokens, void* k_pool_layer, void* v_pool_layer, int64_t num_slots,
+                             int num_kv_heads, int head_dim, float k_scale, float v_scale, void* stream);
+
+/*
+ * pa_paged_decode_ex over FP8 pools: q, out, new_k and new_v in `dtype`
+ * (F32 / F16 / BF16); the fused write quantizes the new token exactly as
+ * pa_kv_scatter_fp8 does.  BF16/F16 with head_dim 64/128, block_size % 16 == 0
+ * and batch <= 1024 run the balanced kernel (FP8 tiles by TMA, dequantized to
+ * f16 in shared memory, f16 tensor-core MMAs with FP32 softmax, k_scale
+ * folded into the score scale and v_scale into the output); F32 and odd
+ * shapes run the CUDA-core kernel.  Workspace as pa_decode_workspace_bytes
+ * with dtype = the query dtype.  Replaces paged_attention_decode_batch_parallel
+ * (kernels/reference/paged_attention.py:178-254) for FP8 pools.
+ */
+PA_API int pa_paged_decode_fp8(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k, const void* new_v,
+                               const int64_t* slot_mapping, void* k_pool_layer, void* v_pool_layer,
+                               int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                               const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
+                               const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
+                               int num_q_heads, float scale, int dtype, float k_scale, float v_scale,
+                               int partition_tokens, int flags, void* workspace, size_t workspace_bytes,
+                               void* stream);
 
 /*
  * Bytes of workspace pa_paged_decode needs for exactly these arguments
@@ -269,6 +308,18 @@ PA_API int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const int
                      int block_size, int num_kv_heads, int head_dim, void* out, int64_t o_s0, int64_t o_s1,
                      int num_seqs, int64_t total_q, int max_q_len, int num_q_heads, float scale, int dtype,
                      int* control, void* stream);
+
+/*
+ * pa_chunk_prefill over FP8 pools (q / out in dtype), on CUDA cores.
+ * Replaces paged_attention_prefill_chunk_tiled
+ * (kernels/reference/paged_attention.py:346-434) for FP8 pools.
+ */
+PA_API int pa_chunk_prefill_fp8(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
+                                const int64_t* context_lens, const int64_t* block_tables, int64_t bt_stride,
+                                int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer,
+                                int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, void* out,
+                                int64_t o_s0, int64_t o_s1, int num_seqs, int64_t total_q, int max_q_len,
+                                int num_q_heads, float scale, int dtype, float k_scale, float v_scale, void* stream);
 
 /*
  * FP32 P.V accumulator: out[b, d] = sum_n p[b, n] * v[b, n, d] for N = 64,

@@ -26,7 +26,9 @@ PA_DECODE_EARLY_INPUTS = 1
 PA_DEVICE_TIMEOUT_TMA = 101
 PA_DEVICE_TIMEOUT_MMA = 102
 
-DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
+DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3, torch.float8_e4m3fn: 4}
+PA_DTYPE_FP8_E4M3 = 4
+FP8_DTYPE = torch.float8_e4m3fn
 
 _c_void_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -73,6 +75,22 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "pa_accumulate_pv": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "pa_decode_noalloc_status": (_i32, [_c_void_p, _c_void_p]),
+    "pa_kv_scatter_fp8": (
+        _i32,
+        [_c_void_p, _i64, _i64, _i64, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p, _i32, _i64,
+         _c_void_p, _c_void_p, _i64, _i32, _i32, _f32, _f32, _c_void_p],
+    ),
+    "pa_paged_decode_fp8": (
+        _i32,
+        [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32,
+         _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _f32, _i32, _f32, _f32, _i32, _i32,
+         _c_void_p, _size, _c_void_p],
+    ),
+    "pa_chunk_prefill_fp8": (
+        _i32,
+        [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64,
+         _i32, _i32, _i32, _c_void_p, _i64, _i64, _i32, _i64, _i32, _i32, _f32, _i32, _f32, _f32, _c_void_p],
+    ),
     "pa_selftest_wait_timeout": (_i32, [_c_void_p, _i64, _c_void_p]),
 }
 

@@ -31,7 +31,8 @@ constexpr int kHeadTile = 8;
 constexpr int kChunk = 256;
 constexpr int kPairsPerThread = kHeadTile * kMaxD / kThreads;  // 16
 
-template <typename T>
+// T: q / out elements; TK: pool elements (T, or FP8 with scales).
+template <typename T, typename TK>
 __global__ void __launch_bounds__(kThreads) attn_generic_kernel(GenericParams p) {
   __shared__ float q_s[kHeadTile][kMaxD];
   __shared__ float sc[kHeadTile][kChunk];
@@ -70,8 +71,8 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(GenericParams p)
   const int nsplits = static_cast<int>((ctx + p.split_tokens - 1) / p.split_tokens);
 
   const T* q = reinterpret_cast<const T*>(p.q);
-  const T* kp = reinterpret_cast<const T*>(p.kp);
-  const T* vp = reinterpret_cast<const T*>(p.vp);
+  const TK* kp = reinterpret_cast<const TK*>(p.kp);
+  const TK* vp = reinterpret_cast<const TK*>(p.vp);
   const int64_t* bt = p.bt + seq * p.bt_stride;
   const int64_t kv_row = (int64_t)p.Hkv * D;
 
@@ -95,12 +96,12 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(GenericParams p)
       const int64_t pos = c0 + j;
       const int64_t pb = bt[pos / p.bs];
       const bool in_pool = pb >= 0 && pb < p.num_blocks;
-      const T* krow = kp + (pb * p.bs + pos % p.bs) * kv_row + (int64_t)kvh * D;
+      const TK* krow = kp + (pb * p.bs + pos % p.bs) * kv_row + (int64_t)kvh * D;
       float part[kHeadTile];
 #pragma unroll
       for (int h = 0; h < kHeadTile; ++h) part[h] = 0.f;
       for (int d = lane; d < D && in_pool; d += 32) {
-        const float kd = Elem<T>::to_f32(krow[d]);
+        const float kd = Elem<TK>::to_f32(krow[d]);
 #pragma unroll
         for (int h = 0; h < kHeadTile; ++h) part[h] = fmaf(q_s[h][d], kd, part[h]);
       }
@@ -147,12 +148,12 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(GenericParams p)
       const int64_t pos = c0 + j;
       const int64_t pb = bt[pos / p.bs];
       if (pb < 0 || pb >= p.num_blocks) continue;  // zero V row contributes nothing
-      const T* vrow = vp + (pb * p.bs + pos % p.bs) * kv_row + (int64_t)kvh * D;
+      const TK* vrow = vp + (pb * p.bs + pos % p.bs) * kv_row + (int64_t)kvh * D;
 #pragma unroll
       for (int i = 0; i < kPairsPerThread; ++i) {
         const int pi = tid + i * kThreads;
         const int h = pi / D, d = pi - h * D;
-        if (h < hn) acc[i] = fmaf(sc[h][j], Elem<T>::to_f32(vrow[d]), acc[i]);
+        if (h < hn) acc[i] = fmaf(sc[h][j], Elem<TK>::to_f32(vrow[d]), acc[i]);
       }
     }
     __syncthreads();
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(GenericParams p)
     for (int i = 0; i < kPairsPerThread; ++i) {
       const int pi = tid + i * kThreads;
       const int h = pi / D, d = pi - h * D;
-      if (h < hn) out[row * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d] = Elem<T>::from_f32(acc[i] / l_s[h]);
+      if (h < hn) out[row * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d] = Elem<T>::from_f32(acc[i] * p.out_scale / l_s[h]);
     }
     return;
   }
@@ -199,24 +200,35 @@ __global__ void __launch_bounds__(kThreads) attn_generic_kernel(GenericParams p)
       l += w * __ldcg(ml + 2 * s + 1);
       o += w * __ldcg(p.part_o + ((base_rh + h) * p.max_splits + s) * D + d);
     }
-    out[row * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d] = Elem<T>::from_f32(o / l);
+    out[row * p.o_s0 + (int64_t)(h0 + h) * p.o_s1 + d] = Elem<T>::from_f32(o * p.out_scale / l);
   }
   if (tid == 0) *ticket = 0;  // ready for the next launch on this workspace
 }
 
 }  // namespace
 
-int launch_attn_generic(const GenericParams& p, int dtype, int splits, cudaStream_t st) {
+int launch_attn_generic(const GenericParams& p, int dtype, int splits, cudaStream_t st, int kv_dtype) {
   if (p.D > kMaxD || p.D <= 0) return PA_ERR_UNSUPPORTED;
   if (p.split_tokens % kChunk != 0 && splits > 1) return PA_ERR_INVALID;
   const int head_tiles = (p.group + kHeadTile - 1) / kHeadTile;
   if (p.num_rows <= 0) return PA_OK;
   if (p.num_rows > 0x7fffffffLL || (int64_t)p.Hkv * head_tiles > 65535 || splits > 65535) return PA_ERR_INVALID;
   dim3 grid(static_cast<unsigned>(p.num_rows), p.Hkv * head_tiles, splits);
+  const bool fp8 = kv_dtype == PA_DTYPE_FP8_E4M3;
+  if (!fp8 && kv_dtype != -1 && kv_dtype != dtype) return PA_ERR_UNSUPPORTED;
   switch (dtype) {
-    case PA_DTYPE_F32: attn_generic_kernel<float><<<grid, kThreads, 0, st>>>(p); break;
-    case PA_DTYPE_F16: attn_generic_kernel<__half><<<grid, kThreads, 0, st>>>(p); break;
-    case PA_DTYPE_BF16: attn_generic_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(p); break;
+    case PA_DTYPE_F32:
+      if (fp8) attn_generic_kernel<float, Fp8E4M3><<<grid, kThreads, 0, st>>>(p);
+      else attn_generic_kernel<float, float><<<grid, kThreads, 0, st>>>(p);
+      break;
+    case PA_DTYPE_F16:
+      if (fp8) attn_generic_kernel<__half, Fp8E4M3><<<grid, kThreads, 0, st>>>(p);
+      else attn_generic_kernel<__half, __half><<<grid, kThreads, 0, st>>>(p);
+      break;
+    case PA_DTYPE_BF16:
+      if (fp8) attn_generic_kernel<__nv_bfloat16, Fp8E4M3><<<grid, kThreads, 0, st>>>(p);
+      else attn_generic_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, kThreads, 0, st>>>(p);
+      break;
     default: return PA_ERR_UNSUPPORTED;
   }
   PA_CHECK_LAUNCH();

@@ -21,7 +21,8 @@ struct GenericParams {
   int64_t num_rows;
   int64_t num_blocks;  // physical blocks per layer; ids outside [0, num_blocks) read as zeros
   int Hq, Hkv, D, bs, group;
-  float scale;
+  float scale;      // score scale (for FP8 pools already times the K scale)
+  float out_scale;  // output factor: 1, or the V scale of an FP8 pool
   int split_tokens, max_splits;
   float* part_ml;  // [rows, Hq, max_splits, 2]
   float* part_o;   // [rows, Hq, max_splits, D]
@@ -49,7 +50,8 @@ inline WorkspaceLayout workspace_layout(int64_t batch, int hq, int d, int splits
   return w;
 }
 
-int launch_attn_generic(const GenericParams& p, int dtype, int splits, cudaStream_t st);
+// dtype: q / out; kv_dtype: the pools (dtype itself, or PA_DTYPE_FP8_E4M3).
+int launch_attn_generic(const GenericParams& p, int dtype, int splits, cudaStream_t st, int kv_dtype = -1);
 int generic_chunk_tokens();
 
 }  // namespace pa

@@ -13,6 +13,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -39,12 +40,30 @@ template <> struct Elem<__nv_bfloat16> {
   __device__ __forceinline__ static __nv_bfloat16 from_f32(float x) { return __float2bfloat16_rn(x); }
 };
 
+// FP8 (e4m3, "fn": no infinities, max finite 448) KV-pool element.  Stored
+// values are the source divided by the pool's scale, saturated to +-448 and
+// rounded to nearest even — clamp(x / scale, -448, 448) cast to
+// torch.float8_e4m3fn; a NaN is stored as 0x7f.  Reads return the stored value; the
+// kernels apply the scale (to the scores for K, to the output for V).
+struct Fp8E4M3 {
+  uint8_t bits;
+};
+template <> struct Elem<Fp8E4M3> {
+  __device__ __forceinline__ static float to_f32(Fp8E4M3 x) {
+    return __half2float(__half(__nv_cvt_fp8_to_halfraw(x.bits, __NV_E4M3)));
+  }
+  __device__ __forceinline__ static Fp8E4M3 from_f32(float x) {
+    return Fp8E4M3{static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3))};
+  }
+};
+
 inline int dtype_size(int dt) {
   switch (dt) {
     case PA_DTYPE_F32: return 4;
     case PA_DTYPE_F16: return 2;
     case PA_DTYPE_BF16: return 2;
     case PA_DTYPE_F64: return 8;
+    case PA_DTYPE_FP8_E4M3: return 1;
     default: return 0;
   }
 }
@@ -239,7 +258,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 
 EncodeTiledFn get_encode_tiled();
 
-// Encodes a 3-D bf16/f16 map (dims innermost first).  Returns PA_OK or
+// Encodes a 3-D map of bf16 / f16 / fp8 (as uint8) elements (dims innermost
+// first).  Returns PA_OK or
 // PA_ERR_CUDA.
 int make_map_3d(CUtensorMap* map, int dtype, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0, uint32_t b1, uint32_t b2,

@@ -38,6 +38,8 @@
 // (sequence, KV head, partition), last-ticket merge).  Everything else (F32,
 // other head dims / block sizes) goes to the CUDA-core kernel in
 // attn_generic.cu.
+#include <type_traits>
+
 #include "attn_generic.cuh"
 
 namespace pa {
@@ -83,20 +85,32 @@ struct WarpState {
     for (int i = 0; i < kDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   }
 
+  // Two adjacent query elements as one MMA register (converted when the MMA
+  // type differs from the query type: FP8 pools run the MMAs in f16).
+  template <typename TQ>
+  __device__ __forceinline__ static uint32_t q_pair(const TQ* p) {
+    if constexpr (std::is_same<TQ, T>::value) {
+      return load_pair_u32(p);
+    } else {
+      return MmaOp<T>::pack(Elem<TQ>::to_f32(p[0]), Elem<TQ>::to_f32(p[1]));
+    }
+  }
+
   // A fragments of Q for rows r0 = lane/4 and r1 = r0 + 8 (zeros for padding).
-  __device__ __forceinline__ static void load_q(uint32_t (&qa_out)[kKK][4], const T* qb, int64_t q_s1, int h0,
+  template <typename TQ>
+  __device__ __forceinline__ static void load_q(uint32_t (&qa_out)[kKK][4], const TQ* qb, int64_t q_s1, int h0,
                                                 int group, int hn, int lane) {
     const int r0 = lane >> 2, cq = 2 * (lane & 3);
     const int e0 = row_head<PK>(r0, group, hn), e1 = row_head<PK>(r0 + 8, group, hn);
-    const T* p0 = qb + (int64_t)(h0 + (e0 < 0 ? 0 : e0)) * q_s1;
-    const T* p1 = qb + (int64_t)(h0 + (e1 < 0 ? 0 : e1)) * q_s1;
+    const TQ* p0 = qb + (int64_t)(h0 + (e0 < 0 ? 0 : e0)) * q_s1;
+    const TQ* p1 = qb + (int64_t)(h0 + (e1 < 0 ? 0 : e1)) * q_s1;
 #pragma unroll
     for (int kk = 0; kk < kKK; ++kk) {
       const int c = kk * 16 + cq;
-      qa_out[kk][0] = e0 >= 0 ? load_pair_u32(p0 + c) : 0u;
-      qa_out[kk][1] = e1 >= 0 ? load_pair_u32(p1 + c) : 0u;
-      qa_out[kk][2] = e0 >= 0 ? load_pair_u32(p0 + c + 8) : 0u;
-      qa_out[kk][3] = e1 >= 0 ? load_pair_u32(p1 + c + 8) : 0u;
+      qa_out[kk][0] = e0 >= 0 ? q_pair(p0 + c) : 0u;
+      qa_out[kk][1] = e1 >= 0 ? q_pair(p1 + c) : 0u;
+      qa_out[kk][2] = e0 >= 0 ? q_pair(p0 + c + 8) : 0u;
+      qa_out[kk][3] = e1 >= 0 ? q_pair(p1 + c + 8) : 0u;
     }
   }
 
@@ -249,19 +263,22 @@ struct WarpState {
     }
   }
 
-  // Final output of a piece that is a whole segment.  Call reduce_l first.
-  __device__ __forceinline__ void store_out(T* ob, int64_t o_s1, int h0, int group, int hn, int lane) const {
+  // Final output of a piece that is a whole segment, times out_scale.  Call
+  // reduce_l first.
+  template <typename TO>
+  __device__ __forceinline__ void store_out(TO* ob, int64_t o_s1, int h0, int group, int hn, int lane,
+                                            float out_scale) const {
     const int r0 = lane >> 2, cq = 2 * (lane & 3);
     const int e0 = row_head<PK>(r0, group, hn), e1 = row_head<PK>(r0 + 8, group, hn);
-    const float i0 = 1.f / l0, i1 = 1.f / l1;
+    const float i0 = out_scale / l0, i1 = out_scale / l1;
 #pragma unroll
     for (int dt = 0; dt < kDT; ++dt) {
       if (e0 >= 0)
         *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e0) * o_s1 + dt * 8 + cq) =
-            MmaOp<T>::pack(o[dt][0] * i0, o[dt][1] * i0);
+            MmaOp<TO>::pack(o[dt][0] * i0, o[dt][1] * i0);
       if (e1 >= 0)
         *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e1) * o_s1 + dt * 8 + cq) =
-            MmaOp<T>::pack(o[dt][2] * i1, o[dt][3] * i1);
+            MmaOp<TO>::pack(o[dt][2] * i1, o[dt][3] * i1);
     }
   }
 };
@@ -311,6 +328,8 @@ struct FlatParams {
   float scale_log2;
   int grid;     // CTAs of the main kernel
   int early;    // PA_DECODE_EARLY_INPUTS: read metadata and pools before the PDL wait
+  float out_scale;  // output factor: 1, or the V scale of an FP8 pool
+  float k_scale, v_scale;  // FP8 pools: the fused write stores x / scale
   float* part;  // [grid][2][16][D + 4] records of segments shared with other CTAs
   int* status;
   // Fused KV write (all null when the new token is already in the pools):
@@ -372,29 +391,72 @@ __device__ __forceinline__ void seg_heads(const FlatParams& p, int segx, int& kv
   }
 }
 
-template <int D, int PK, int NW, int STAGES>
+// KV8: FP8 pools.  A ring stage then holds the FP8 tiles (16 tokens x 64
+// bytes, 1 KB, unswizzled), and each warp has a dequant buffer of NSUB
+// sub-blocks in the 16-bit swizzled layout the MMA loads read.
+template <int D, int PK, int NW, int STAGES, int NSUB = 1, bool KV8 = false>
 struct FlatCfg {
   static constexpr int kColTiles = D / 64;
-  static constexpr int kStageBytes = 2 * kColTiles * PK * kTileBytes;  // K + V of one sub-block
+  static constexpr int kTile8 = kSub * 64;  // one FP8 tile: 16 tokens x 64 bytes
+  static constexpr int kStage16 = 2 * kColTiles * PK * kTileBytes;  // K + V of one sub-block, 16-bit
+  static constexpr int kStageBytes = KV8 ? 2 * kColTiles * PK * kTile8 : kStage16;
   static constexpr int kRingBytes = NW * STAGES * kStageBytes;
+  static constexpr int kDeqBytes = KV8 ? NW * NSUB * kStage16 : 0;  // per-warp dequant buffers
   static constexpr int kRec = D + 4;  // record floats per row
   static constexpr int kRecBytes = 16 * kRec * 4;
   static constexpr int kStagingBytes = NW * kRecBytes;  // first-piece record per warp
   static constexpr int kPrefixBytes = (kFlatMaxBatch + 1) * 4;
-  static constexpr int kOffStaging = kRingBytes;
+  static constexpr int kOffDeq = kRingBytes;
+  static constexpr int kOffStaging = kOffDeq + kDeqBytes;
   static constexpr int kOffPrefix = kOffStaging + kStagingBytes;
   static constexpr int kOffBars = kOffPrefix + ((kPrefixBytes + 15) & ~15);
   static constexpr size_t kSmem = 1024 + kOffBars + NW * STAGES * 8 + 64;
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
-  static_assert(STAGES * kStageBytes >= kRecBytes, "a warp's ring holds its last-piece record at the end");
+  // At the end a warp's ring (its dequant buffer with FP8) holds its last-piece record.
+  static constexpr int kRecAreaBytes = KV8 ? NSUB * kStage16 : STAGES * kStageBytes;
+  static_assert(kRecAreaBytes >= kRecBytes, "a warp's ring holds its last-piece record at the end");
+  __device__ __forceinline__ static int rec_area(int warp) {
+    return KV8 ? kOffDeq + warp * NSUB * kStage16 : warp * STAGES * kStageBytes;
+  }
 };
 
-template <typename T, int D, int PK, int NW, int STAGES, int NSUB, int CTAS>
+// FP8 stage -> 16-bit tiles in the swizzled layout of the BF16/F16 path
+// (f16 values: exact for every e4m3 value).  Lane i converts 16-byte chunks
+// i, i + 32, ...: chunk c of FP8 tile t is row (c % 64) / 4, bytes
+// 16 * (c % 4) .. + 16, and becomes two 16-byte chunks of 16-bit tile t.
+template <int NTILES>
+__device__ __forceinline__ void dequant_fp8_stage(const uint8_t* src, uint8_t* dst, int lane) {
+#pragma unroll
+  for (int k = 0; k < NTILES * 64 / 32; ++k) {
+    const int c = lane + 32 * k;
+    const int t = c >> 6, r = (c & 63) >> 2, cc = c & 3;
+    const int4 raw = *reinterpret_cast<const int4*>(src + t * kSub * 64 + r * 64 + cc * 16);
+    const uint32_t w[4] = {static_cast<uint32_t>(raw.x), static_cast<uint32_t>(raw.y), static_cast<uint32_t>(raw.z),
+                           static_cast<uint32_t>(raw.w)};
+    uint32_t h[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] & 0xffffu), __NV_E4M3);
+      const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] >> 16), __NV_E4M3);
+      h[2 * i] = static_cast<uint32_t>(lo.x) | (static_cast<uint32_t>(lo.y) << 16);
+      h[2 * i + 1] = static_cast<uint32_t>(hi.x) | (static_cast<uint32_t>(hi.y) << 16);
+    }
+    uint8_t* d = dst + t * kTileBytes + r * kTileRowBytes;
+    *reinterpret_cast<int4*>(d + (((2 * cc) ^ (r & 7)) << 4)) = make_int4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<int4*>(d + (((2 * cc + 1) ^ (r & 7)) << 4)) = make_int4(h[4], h[5], h[6], h[7]);
+  }
+}
+
+// TQ: query / output elements.  KV8: FP8 pools, MMAs in f16 on the
+// dequantized tiles (T is the MMA element type).
+template <typename TQ, int D, int PK, int NW, int STAGES, int NSUB, int CTAS, bool KV8>
 __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                                                    const __grid_constant__ CUtensorMap tmap_v,
                                                                    FlatParams p) {
-  using C = FlatCfg<D, PK, NW, STAGES>;
+  using T = typename std::conditional<KV8, __half, TQ>::type;
+  using C = FlatCfg<D, PK, NW, STAGES, NSUB, KV8>;
   using WS = WarpState<T, D, PK>;
+  constexpr int kTileX = KV8 ? C::kTile8 : kTileBytes;  // bytes of one staged tile
   static_assert(STAGES >= NSUB, "a consume step takes NSUB staged sub-blocks");
   constexpr int NT = NW * 32;
   constexpr int kRec = C::kRec;
@@ -511,8 +573,8 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
       for (int ct = 0; ct < C::kColTiles; ++ct)
 #pragma unroll
         for (int h = 0; h < PK; ++h) {
-          tma_load_3d(st + (ct * PK + h) * kTileBytes, &tmap_k, &wbar[stage], ct * 64, kv + h, y);
-          tma_load_3d(st + ((C::kColTiles + ct) * PK + h) * kTileBytes, &tmap_v, &wbar[stage], ct * 64, kv + h, y);
+          tma_load_3d(st + (ct * PK + h) * kTileX, &tmap_k, &wbar[stage], ct * 64, kv + h, y);
+          tma_load_3d(st + ((C::kColTiles + ct) * PK + h) * kTileX, &tmap_v, &wbar[stage], ct * 64, kv + h, y);
         }
     }
   };
@@ -520,8 +582,8 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
   for (; issued < STAGES && issued < nj; ++issued) issue(issued);
   if (p.early) grid_dep_wait();
 
-  const T* qbase = reinterpret_cast<const T*>(p.q);
-  T* out = reinterpret_cast<T*>(p.out);
+  const TQ* qbase = reinterpret_cast<const TQ*>(p.q);
+  TQ* out = reinterpret_cast<TQ*>(p.out);
   WS ws;
   int jc = 0;  // sub-blocks of this slice consumed so far
   bool ok = true;
@@ -531,7 +593,7 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
     pc = seg_at(pre, p.B, p.SPS, lo);
     int kvh0, h0, hn;
     seg_heads<PK>(p, pc.segx, kvh0, h0, hn);
-    WS::load_q(ws.qa, qbase + (int64_t)pc.b * p.q_s0, p.q_s1, h0, p.group, hn, lane);
+    WS::template load_q<TQ>(ws.qa, qbase + (int64_t)pc.b * p.q_s0, p.q_s1, h0, p.group, hn, lane);
   }
   int64_t x = lo;
   while (x < hi) {
@@ -549,7 +611,7 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
       nc = seg_at(pre, p.B, p.SPS, pend);
       int kvn, h0n, hnn;
       seg_heads<PK>(p, nc.segx, kvn, h0n, hnn);
-      WS::load_q(qn, qbase + (int64_t)nc.b * p.q_s0, p.q_s1, h0n, p.group, hnn, lane);
+      WS::template load_q<TQ>(qn, qbase + (int64_t)nc.b * p.q_s0, p.q_s1, h0n, p.group, hnn, lane);
     }
     ws.reset();
     const int jend = static_cast<int>(pend - lo);
@@ -563,7 +625,14 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
           const int j = jc + u;
           const int stage = j % STAGES;
           if (ok) ok = mbar_wait(&wbar[stage], (j / STAGES) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-          stg[u] = smem_u32(ring + stage * C::kStageBytes);
+          // The tiles the MMAs read: the stage itself, or (FP8) its dequantized copy.
+          uint8_t* tiles = ring + stage * C::kStageBytes;
+          if (KV8) {
+            uint8_t* dq = smem + C::kOffDeq + (warp * NSUB + u) * C::kStage16;
+            if (ok) dequant_fp8_stage<2 * C::kColTiles * PK>(tiles, dq, lane);
+            tiles = dq;
+          }
+          stg[u] = smem_u32(tiles);
           const int64_t sub = lo + j - pc.start;
           valid[u] = static_cast<int>(min((int64_t)kSub, ctx - sub * kSub));
           if (p.new_k != nullptr && (sub + 1) * kSub >= ctx) {
@@ -582,30 +651,60 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
               const int kv = kvct / C::kColTiles, ct = kvct - kv * C::kColTiles;
               const int64_t src = ((int64_t)b * p.Hkv + kvh0 + h) * D + ct * 64 + cc * 8;
               const int4 val =
-                  __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const T*>(kv ? p.new_v : p.new_k) + src));
-              uint8_t* dst = ring + stage * C::kStageBytes + t * kTileBytes + r * 128 + ((cc ^ (r & 7)) << 4);
-              *reinterpret_cast<int4*>(dst) = val;
-              if (store_pool && slot >= 0 && slot < p.num_slots)
-                *reinterpret_cast<int4*>(reinterpret_cast<T*>(kv ? p.v_pool : p.k_pool) +
-                                         (slot * p.Hkv + kvh0 + h) * D + ct * 64 + cc * 8) = val;
+                  __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const TQ*>(kv ? p.new_v : p.new_k) + src));
+              uint8_t* dst = tiles + t * kTileBytes + r * 128 + ((cc ^ (r & 7)) << 4);
+              const int64_t pool_el = (slot * p.Hkv + kvh0 + h) * D + ct * 64 + cc * 8;
+              if (KV8) {
+                // Quantize as the FP8 scatter does (x / scale, saturated,
+                // nearest even), store the bytes, and patch their f16 values.
+                const TQ* e = reinterpret_cast<const TQ*>(&val);
+                const float sc = kv ? p.v_scale : p.k_scale;
+                uint32_t f8[2] = {0u, 0u}, hv[4];
+#pragma unroll
+                for (int k2 = 0; k2 < 8; k2 += 2) {
+                  const uint32_t b0 = __nv_cvt_float_to_fp8(__fdiv_rn(Elem<TQ>::to_f32(e[k2]), sc), __NV_SATFINITE,
+                                                            __NV_E4M3);
+                  const uint32_t b1 = __nv_cvt_float_to_fp8(__fdiv_rn(Elem<TQ>::to_f32(e[k2 + 1]), sc),
+                                                            __NV_SATFINITE, __NV_E4M3);
+                  f8[k2 >> 2] |= (b0 | (b1 << 8)) << (8 * (k2 & 3));
+                  const __half2_raw hh =
+                      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(b0 | (b1 << 8)), __NV_E4M3);
+                  hv[k2 >> 1] = static_cast<uint32_t>(hh.x) | (static_cast<uint32_t>(hh.y) << 16);
+                }
+                *reinterpret_cast<int4*>(dst) = make_int4(hv[0], hv[1], hv[2], hv[3]);
+                if (store_pool && slot >= 0 && slot < p.num_slots)
+                  *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(kv ? p.v_pool : p.k_pool) + pool_el) =
+                      make_uint2(f8[0], f8[1]);
+              } else {
+                *reinterpret_cast<int4*>(dst) = val;
+                if (store_pool && slot >= 0 && slot < p.num_slots)
+                  *reinterpret_cast<int4*>(reinterpret_cast<TQ*>(kv ? p.v_pool : p.k_pool) + pool_el) = val;
+              }
             }
-            fence_proxy_async_smem();  // before the stage is refilled by TMA
+            if (!KV8) fence_proxy_async_smem();  // before the stage is refilled by TMA
             __syncwarp();
           }
         }
       }
       if (!ok) break;
+      if (KV8) {
+        // The FP8 stages are free once dequantized: refill them before the MMAs.
+        __syncwarp();
+        for (int u = 0; u < n; ++u)
+          if (issued < nj) issue(issued++);
+      }
       if (n == NSUB) ws.template consume<NSUB>(stg, valid, p.scale_log2, lane);
       else ws.template consume<1>(stg, valid, p.scale_log2, lane);
       __syncwarp();
-      for (int u = 0; u < n; ++u)
-        if (issued < nj) issue(issued++);
+      if (!KV8)
+        for (int u = 0; u < n; ++u)
+          if (issued < nj) issue(issued++);
       jc += n;
     }
     if (!ok) break;
     ws.reduce_l();
     if (whole) {
-      ws.store_out(out + (int64_t)b * p.o_s0, p.o_s1, h0, p.group, hn, lane);
+      ws.store_out(out + (int64_t)b * p.o_s0, p.o_s1, h0, p.group, hn, lane, p.out_scale);
     } else if (x == lo) {  // cut at the slice start: park the record until the end
       ws.store(staging + warp * 16 * kRec, lane);
       first_sid = b * p.SPS + segx;
@@ -628,9 +727,9 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
     for (int j = jc; j < issued; ++j) mbar_wait(&wbar[j % STAGES], (j / STAGES) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
     first_sid = last_sid = -1;
   }
-  // This warp's copies have all landed: its ring is free for the last-piece
-  // record.
-  if (last_sid >= 0) ws.store(reinterpret_cast<float*>(ring), lane);
+  // This warp's copies have all landed: its ring (or dequant buffer) is free
+  // for the last-piece record.
+  if (last_sid >= 0) ws.store(reinterpret_cast<float*>(smem + C::rec_area(warp)), lane);
   if (lane == 0) {
     ent_seg[2 * warp] = first_sid;
     ent_seg[2 * warp + 1] = last_sid;
@@ -654,9 +753,9 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
         ++n;
         prev = sid;
       }
-      // Entry f's record: a warp's ring (last piece) or its staging slot.
-      run_rec[n - 1][run_nrec[n - 1]++] = (f & 1) ? (f >> 1) * STAGES * C::kStageBytes / 4
-                                                  : (C::kOffStaging + (f >> 1) * C::kRecBytes) / 4;
+      // Entry f's record: the warp's record area (last piece) or its staging slot.
+      run_rec[n - 1][run_nrec[n - 1]++] =
+          (f & 1) ? C::rec_area(f >> 1) / 4 : (C::kOffStaging + (f >> 1) * C::kRecBytes) / 4;
     }
     nruns_s = n;
   }
@@ -690,7 +789,7 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
       axpy8(wt, *reinterpret_cast<const float4*>(rec + 4 + d), *reinterpret_cast<const float4*>(rec + 8 + d), acc);
     }
     if (S.start >= clo && S.end <= chi) {
-      store8<T>(out + (int64_t)S.b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d, acc, 1.f / l);
+      store8<TQ>(out + (int64_t)S.b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d, acc, p.out_scale / l);
     } else {
       float* row = p.part + (((int64_t)c * 2 + (S.start < clo ? 0 : 1)) * 16 + r) * kRec;
       if (d == 0) *reinterpret_cast<float2*>(row) = make_float2(mx, l);
@@ -830,7 +929,7 @@ __global__ void __launch_bounds__(kCombineThreads, 8) decode_combine_kernel(Flat
   }
   if (hh < 0) return;
   T* out = reinterpret_cast<T*>(p.out);
-  store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d, acc, 1.f / lrun);
+  store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d, acc, p.out_scale / lrun);
 }
 
 // Merge `nw` warp records (m, l, O) of row h, column d (log2 domain).
@@ -1009,11 +1108,16 @@ int current_device() {
 // merge tail overlap the other's streaming and, with PDL, the next kernel's
 // CTAs move in as soon as one exits.  A stage is one sub-block of every head
 // of the pack: 8 KB (D = 64, PK = 2) to 16 KB (D = 128, PK = 2).
-template <int D, int PK> struct FlatShape;
+// FP8 pools halve a stage, so they take one more ring stage.
+template <int D, int PK, bool KV8 = false> struct FlatShape;
 template <> struct FlatShape<64, 2> { static constexpr int NW = 4, ST = 2, NSUB = 1; };
 template <> struct FlatShape<64, 1> { static constexpr int NW = 4, ST = 4, NSUB = 2; };
 template <> struct FlatShape<128, 2> { static constexpr int NW = 2, ST = 2, NSUB = 1; };
 template <> struct FlatShape<128, 1> { static constexpr int NW = 2, ST = 4, NSUB = 2; };
+template <> struct FlatShape<64, 2, true> { static constexpr int NW = 4, ST = 3, NSUB = 1; };
+template <> struct FlatShape<64, 1, true> { static constexpr int NW = 4, ST = 4, NSUB = 2; };
+template <> struct FlatShape<128, 2, true> { static constexpr int NW = 2, ST = 3, NSUB = 1; };
+template <> struct FlatShape<128, 1, true> { static constexpr int NW = 2, ST = 4, NSUB = 2; };
 constexpr int kFlatCtasPerSm = 2;
 constexpr int kSplitNW = 4, kSplitST = 4;
 
@@ -1032,11 +1136,11 @@ bool set_smem_attr(K kern, size_t bytes, bool* done) {
   return true;
 }
 
-template <typename T, int D, int PK>
+template <typename T, int D, int PK, bool KV8>
 int launch_flat(const FlatParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int grid, cudaStream_t st) {
-  using S = FlatShape<D, PK>;
-  using C = FlatCfg<D, PK, S::NW, S::ST>;
-  auto kern = decode_flat_kernel<T, D, PK, S::NW, S::ST, S::NSUB, kFlatCtasPerSm>;
+  using S = FlatShape<D, PK, KV8>;
+  using C = FlatCfg<D, PK, S::NW, S::ST, S::NSUB, KV8>;
+  auto kern = decode_flat_kernel<T, D, PK, S::NW, S::ST, S::NSUB, kFlatCtasPerSm, KV8>;
   static bool done[64] = {};
   if (!set_smem_attr(kern, C::kSmem, done)) return PA_ERR_CUDA;
   const int r = launch_pdl(kern, dim3(grid), dim3(S::NW * 32), C::kSmem, st, tk, tv, p);
@@ -1166,7 +1270,7 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
                 int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
                 int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
                 void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused,
-                int flags = 0);
+                int flags = 0, int kv_dtype = -1, float k_scale = 1.f, float v_scale = 1.f);
 
 }  // namespace
 }  // namespace pa
@@ -1251,7 +1355,7 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
                 int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
                 int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
                 void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused,
-                int flags) {
+                int flags, int kv_dtype, float k_scale, float v_scale) {
   if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0 ||
       block_size <= 0 || num_blocks <= 0 || bt_width <= 0 || partition_tokens < 0 || (flags & ~PA_DECODE_EARLY_INPUTS))
     return PA_ERR_INVALID;
@@ -1261,6 +1365,10 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
     return PA_ERR_INVALID;
   if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16) return PA_ERR_UNSUPPORTED;
   if (batch > 65535) return PA_ERR_INVALID;
+  const bool kv8 = kv_dtype == PA_DTYPE_FP8_E4M3;
+  if (kv_dtype != -1 && !kv8) return PA_ERR_UNSUPPORTED;
+  if (kv8 && (!(k_scale > 0.f) || !(v_scale > 0.f) || isinf(k_scale) || isinf(v_scale))) return PA_ERR_INVALID;
+  if (!kv8) k_scale = v_scale = 1.f;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int group = num_q_heads / num_kv_heads;
   DecodePlan pl =
@@ -1285,18 +1393,24 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
   int* status = reinterpret_cast<int*>(ws);
 
   if (pl.kind == DecodePlan::kFlat || pl.kind == DecodePlan::kSplit) {
+    if (kv8 && pl.kind != DecodePlan::kFlat) return PA_ERR_UNSUPPORTED;  // batches > 1024 with FP8 pools
     CUtensorMap tk, tv;
     const uint64_t slots = static_cast<uint64_t>(num_blocks) * block_size;
-    const uint64_t s1b = static_cast<uint64_t>(head_dim) * 2;
+    const uint64_t s1b = static_cast<uint64_t>(head_dim) * (kv8 ? 1 : 2);
     const uint64_t s2b = s1b * num_kv_heads;
-    // Rows of one KV head are 128 B with a Hkv*128 B stride; a wider L2
-    // promotion would drag the other heads' rows in ahead of their readers.
-    if (make_map_3d(&tk, dtype, k_pool_layer, head_dim, num_kv_heads, slots, s1b, s2b, 64, 1, 16,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B) != PA_OK ||
-        make_map_3d(&tv, dtype, v_pool_layer, head_dim, num_kv_heads, slots, s1b, s2b, 64, 1, 16,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B) != PA_OK)
+    const int map_dtype = kv8 ? PA_DTYPE_FP8_E4M3 : dtype;
+    // Rows of one KV head are 128 B (64 B with FP8) with a Hkv-row stride; a
+    // wider L2 promotion would drag the other heads' rows in ahead of their
+    // readers.  FP8 tiles land unswizzled (64-byte rows); the warp rewrites
+    // them as swizzled f16 tiles.
+    const CUtensorMapSwizzle swz_mode = kv8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
+    const CUtensorMapL2promotion l2p = kv8 ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B : CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+    if (make_map_3d(&tk, map_dtype, k_pool_layer, head_dim, num_kv_heads, slots, s1b, s2b, 64, 1, 16, swz_mode,
+                    l2p) != PA_OK ||
+        make_map_3d(&tv, map_dtype, v_pool_layer, head_dim, num_kv_heads, slots, s1b, s2b, 64, 1, 16, swz_mode,
+                    l2p) != PA_OK)
       return PA_ERR_CUDA;
-    const float scale_log2 = scale * 1.4426950408889634f;
+    const float scale_log2 = scale * k_scale * 1.4426950408889634f;
     if (pl.kind == DecodePlan::kFlat) {
       FlatParams p;
       p.q = q;
@@ -1320,6 +1434,9 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
       p.scale_log2 = scale_log2;
       p.grid = pl.grid;
       p.early = (flags & PA_DECODE_EARLY_INPUTS) ? 1 : 0;
+      p.out_scale = v_scale;
+      p.k_scale = k_scale;
+      p.v_scale = v_scale;
       p.part = reinterpret_cast<float*>(ws + 256 + align256(sizeof(int) * (size_t)batch * num_q_heads));
       p.status = status;
       p.new_k = fw ? fw->new_k : nullptr;
@@ -1330,15 +1447,29 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
       p.num_slots = static_cast<int64_t>(num_blocks) * block_size;
       if (fused != nullptr) *fused = fw != nullptr;
       const int g = pl.grid;
-      if (dtype == PA_DTYPE_BF16) {
-        using B16 = __nv_bfloat16;
+      using B16 = __nv_bfloat16;
+      if (kv8) {
+        if (dtype == PA_DTYPE_BF16) {
+          if (head_dim == 64)
+            return pk2 ? launch_flat<B16, 64, 2, true>(p, tk, tv, g, st) : launch_flat<B16, 64, 1, true>(p, tk, tv, g, st);
+          return pk2 ? launch_flat<B16, 128, 2, true>(p, tk, tv, g, st) : launch_flat<B16, 128, 1, true>(p, tk, tv, g, st);
+        }
         if (head_dim == 64)
-          return pk2 ? launch_flat<B16, 64, 2>(p, tk, tv, g, st) : launch_flat<B16, 64, 1>(p, tk, tv, g, st);
-        return pk2 ? launch_flat<B16, 128, 2>(p, tk, tv, g, st) : launch_flat<B16, 128, 1>(p, tk, tv, g, st);
+          return pk2 ? launch_flat<__half, 64, 2, true>(p, tk, tv, g, st)
+                     : launch_flat<__half, 64, 1, true>(p, tk, tv, g, st);
+        return pk2 ? launch_flat<__half, 128, 2, true>(p, tk, tv, g, st)
+                   : launch_flat<__half, 128, 1, true>(p, tk, tv, g, st);
+      }
+      if (dtype == PA_DTYPE_BF16) {
+        if (head_dim == 64)
+          return pk2 ? launch_flat<B16, 64, 2, false>(p, tk, tv, g, st) : launch_flat<B16, 64, 1, false>(p, tk, tv, g, st);
+        return pk2 ? launch_flat<B16, 128, 2, false>(p, tk, tv, g, st) : launch_flat<B16, 128, 1, false>(p, tk, tv, g, st);
       }
       if (head_dim == 64)
-        return pk2 ? launch_flat<__half, 64, 2>(p, tk, tv, g, st) : launch_flat<__half, 64, 1>(p, tk, tv, g, st);
-      return pk2 ? launch_flat<__half, 128, 2>(p, tk, tv, g, st) : launch_flat<__half, 128, 1>(p, tk, tv, g, st);
+        return pk2 ? launch_flat<__half, 64, 2, false>(p, tk, tv, g, st)
+                   : launch_flat<__half, 64, 1, false>(p, tk, tv, g, st);
+      return pk2 ? launch_flat<__half, 128, 2, false>(p, tk, tv, g, st)
+                 : launch_flat<__half, 128, 1, false>(p, tk, tv, g, st);
     }
     if (pl.splits > 65535) return PA_ERR_INVALID;
     const WorkspaceLayout wl = workspace_layout(batch, num_q_heads, head_dim, pl.splits);
@@ -1395,15 +1526,61 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
   g.D = head_dim;
   g.bs = block_size;
   g.group = group;
-  g.scale = scale;
+  g.scale = scale * k_scale;
+  g.out_scale = v_scale;
   g.split_tokens = pl.split_tokens;
   g.max_splits = pl.splits;
   g.part_ml = pl.splits > 1 ? reinterpret_cast<float*>(ws + wl.part_ml) : nullptr;
   g.part_o = pl.splits > 1 ? reinterpret_cast<float*>(ws + wl.part_o) : nullptr;
   g.tickets = pl.splits > 1 ? reinterpret_cast<int*>(ws + wl.tickets) : nullptr;
   g.status = status;
-  return launch_attn_generic(g, dtype, pl.splits, st);
+  return launch_attn_generic(g, dtype, pl.splits, st, kv8 ? PA_DTYPE_FP8_E4M3 : dtype);
 }
 
 }  // namespace
 }  // namespace pa
+
+extern "C" int pa_kv_scatter_fp8(const void* k, int64_t k_s0, int64_t k_s1, int64_t k_s2, const void* v,
+                                 int64_t v_s0, int64_t v_s1, int64_t v_s2, int src_dtype, const void* slot_mapping,
+                                 int slot_is_int64, int64_t num_tokens, void* k_pool_layer, void* v_pool_layer,
+                                 int64_t num_slots, int num_kv_heads, int head_dim, float k_scale, float v_scale,
+                                 void* stream);
+
+extern "C" int pa_paged_decode_fp8(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k, const void* new_v,
+                                   const int64_t* slot_mapping, void* k_pool_layer, void* v_pool_layer,
+                                   int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                                   const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
+                                   const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
+                                   int num_q_heads, float scale, int dtype, float k_scale, float v_scale,
+                                   int partition_tokens, int flags, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  using namespace pa;
+  if (batch < 0 || (flags & ~PA_DECODE_EARLY_INPUTS)) return PA_ERR_INVALID;
+  if (batch == 0) return PA_OK;
+  const bool write = new_k != nullptr || new_v != nullptr || slot_mapping != nullptr;
+  if (write) {
+    if (new_k == nullptr || new_v == nullptr || slot_mapping == nullptr || partition_tokens != 0)
+      return PA_ERR_INVALID;
+    if (!((reinterpret_cast<uintptr_t>(new_k) | reinterpret_cast<uintptr_t>(new_v)) & 15)) {
+      FusedWrite fw{new_k, new_v, slot_mapping};
+      bool fused = false;
+      const int r = decode_impl(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads,
+                                head_dim, block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch,
+                                num_q_heads, scale, dtype, 0, workspace, workspace_bytes, stream, &fw, &fused, flags,
+                                PA_DTYPE_FP8_E4M3, k_scale, v_scale);
+      if (r != PA_OK || fused) return r;
+    }
+    // Not fusable here: quantizing scatter, then decode (which then waits
+    // before its first read: the scatter just wrote pool rows).
+    const int64_t s1 = head_dim, s0 = (int64_t)num_kv_heads * head_dim;
+    const int r = pa_kv_scatter_fp8(new_k, s0, s1, 1, new_v, s0, s1, 1, dtype, slot_mapping, 1, batch, k_pool_layer,
+                                    v_pool_layer, num_blocks * (int64_t)block_size, num_kv_heads, head_dim, k_scale,
+                                    v_scale, stream);
+    if (r != PA_OK) return r;
+    flags = 0;
+  }
+  return decode_impl(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads, head_dim,
+                     block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch, num_q_heads, scale, dtype,
+                     partition_tokens, workspace, workspace_bytes, stream, nullptr, nullptr, flags, PA_DTYPE_FP8_E4M3,
+                     k_scale, v_scale);
+}

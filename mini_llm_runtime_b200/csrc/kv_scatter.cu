@@ -74,6 +74,49 @@ __global__ void scatter_rows_cvt(const S* __restrict__ k, int64_t ks0, int64_t k
   }
 }
 
+// FP8 pools: element = clamp(x / scale, -448, 448) rounded to nearest even,
+// the division in FP32 (x converted first, f64 through f32).
+template <typename S, typename I>
+__global__ void scatter_rows_fp8(const S* __restrict__ k, int64_t ks0, int64_t ks1, int64_t ks2,
+                                 const S* __restrict__ v, int64_t vs0, int64_t vs1, int64_t vs2,
+                                 const void* __restrict__ slots, int64_t num_tokens, Fp8E4M3* __restrict__ k_pool,
+                                 Fp8E4M3* __restrict__ v_pool, int64_t num_slots, int hkv, int d, float k_scale,
+                                 float v_scale) {
+  grid_dep_wait();  // PDL launch: the previous kernel has finished
+  grid_dep_launch();
+  const int64_t row = static_cast<int64_t>(hkv) * d;
+  const int64_t total = num_tokens * row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / row;
+    const int64_t r = i - t * row;
+    const int h = static_cast<int>(r / d);
+    const int e = static_cast<int>(r - (int64_t)h * d);
+    const int64_t slot = load_slot<I>(slots, t);
+    if (slot < 0 || slot >= num_slots) continue;
+    const float kv = __fdiv_rn(SrcLoad<S>::get(k + t * ks0 + h * ks1 + e * ks2), k_scale);
+    const float vv = __fdiv_rn(SrcLoad<S>::get(v + t * vs0 + h * vs1 + e * vs2), v_scale);
+    k_pool[slot * row + r] = Elem<Fp8E4M3>::from_f32(kv);
+    v_pool[slot * row + r] = Elem<Fp8E4M3>::from_f32(vv);
+  }
+}
+
+template <typename S>
+int launch_fp8_idx(const void* k, int64_t ks0, int64_t ks1, int64_t ks2, const void* v, int64_t vs0, int64_t vs1,
+                   int64_t vs2, const void* slots, int slot64, int64_t T, void* kp, void* vp, int64_t num_slots,
+                   int hkv, int d, float k_scale, float v_scale, cudaStream_t st) {
+  const int64_t total = T * hkv * d;
+  const int threads = 256;
+  int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (slot64)
+    return launch_pdl(scatter_rows_fp8<S, int64_t>, dim3((unsigned)blocks), dim3(threads), 0, st, (const S*)k, ks0,
+                      ks1, ks2, (const S*)v, vs0, vs1, vs2, slots, T, (Fp8E4M3*)kp, (Fp8E4M3*)vp, num_slots, hkv, d,
+                      k_scale, v_scale);
+  return launch_pdl(scatter_rows_fp8<S, int32_t>, dim3((unsigned)blocks), dim3(threads), 0, st, (const S*)k, ks0,
+                    ks1, ks2, (const S*)v, vs0, vs1, vs2, slots, T, (Fp8E4M3*)kp, (Fp8E4M3*)vp, num_slots, hkv, d,
+                    k_scale, v_scale);
+}
+
 // f32 -> f32 and f64 -> f32 keep full precision without the float detour
 // mattering (identity / single rounding), so the generic kernel is exact.
 
@@ -117,6 +160,39 @@ int launch_cvt_src(int src_dtype, const void* k, int64_t ks0, int64_t ks1, int64
 }  // namespace
 }  // namespace pa
 
+extern "C" int pa_kv_scatter_fp8(const void* k, int64_t k_s0, int64_t k_s1, int64_t k_s2, const void* v,
+                                 int64_t v_s0, int64_t v_s1, int64_t v_s2, int src_dtype, const void* slot_mapping,
+                                 int slot_is_int64, int64_t num_tokens, void* k_pool_layer, void* v_pool_layer,
+                                 int64_t num_slots, int num_kv_heads, int head_dim, float k_scale, float v_scale,
+                                 void* stream) {
+  using namespace pa;
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || num_slots < 0) return PA_ERR_INVALID;
+  if (!(k_scale > 0.f) || !(v_scale > 0.f) || isinf(k_scale) || isinf(v_scale)) return PA_ERR_INVALID;
+  if (num_tokens == 0) return PA_OK;
+  if (k == nullptr || v == nullptr || slot_mapping == nullptr || k_pool_layer == nullptr || v_pool_layer == nullptr)
+    return PA_ERR_INVALID;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (src_dtype) {
+    case PA_DTYPE_F32:
+      return launch_fp8_idx<float>(k, k_s0, k_s1, k_s2, v, v_s0, v_s1, v_s2, slot_mapping, slot_is_int64, num_tokens,
+                                   k_pool_layer, v_pool_layer, num_slots, num_kv_heads, head_dim, k_scale, v_scale, st);
+    case PA_DTYPE_F16:
+      return launch_fp8_idx<__half>(k, k_s0, k_s1, k_s2, v, v_s0, v_s1, v_s2, slot_mapping, slot_is_int64, num_tokens,
+                                    k_pool_layer, v_pool_layer, num_slots, num_kv_heads, head_dim, k_scale, v_scale,
+                                    st);
+    case PA_DTYPE_BF16:
+      return launch_fp8_idx<__nv_bfloat16>(k, k_s0, k_s1, k_s2, v, v_s0, v_s1, v_s2, slot_mapping, slot_is_int64,
+                                           num_tokens, k_pool_layer, v_pool_layer, num_slots, num_kv_heads, head_dim,
+                                           k_scale, v_scale, st);
+    case PA_DTYPE_F64:
+      return launch_fp8_idx<double>(k, k_s0, k_s1, k_s2, v, v_s0, v_s1, v_s2, slot_mapping, slot_is_int64, num_tokens,
+                                    k_pool_layer, v_pool_layer, num_slots, num_kv_heads, head_dim, k_scale, v_scale,
+                                    st);
+    default:
+      return PA_ERR_UNSUPPORTED;
+  }
+}
+
 extern "C" int pa_kv_scatter(const void* k, int64_t k_s0, int64_t k_s1, int64_t k_s2, const void* v, int64_t v_s0,
                              int64_t v_s1, int64_t v_s2, int src_dtype, const void* slot_mapping, int slot_is_int64,
                              int64_t num_tokens, void* k_pool_layer, void* v_pool_layer, int64_t num_slots,
@@ -126,8 +202,9 @@ extern "C" int pa_kv_scatter(const void* k, int64_t k_s0, int64_t k_s1, int64_t 
   if (num_tokens == 0) return PA_OK;  // empty writes are allowed (paged_kv_cache.py:203)
   if (k == nullptr || v == nullptr || slot_mapping == nullptr || k_pool_layer == nullptr || v_pool_layer == nullptr)
     return PA_ERR_INVALID;
-  if (dtype_size(src_dtype) == 0 || dtype_size(pool_dtype) == 0 || pool_dtype == PA_DTYPE_F64)
-    return PA_ERR_UNSUPPORTED;
+  if (dtype_size(src_dtype) == 0 || dtype_size(pool_dtype) == 0 || pool_dtype == PA_DTYPE_F64 ||
+      src_dtype == PA_DTYPE_FP8_E4M3 || pool_dtype == PA_DTYPE_FP8_E4M3)
+    return PA_ERR_UNSUPPORTED;  // FP8 pools take pa_kv_scatter_fp8 (they need a scale)
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int es = dtype_size(pool_dtype);
   const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;

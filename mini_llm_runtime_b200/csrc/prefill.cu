@@ -12,12 +12,14 @@
 #include "attn_generic.cuh"
 #include "prefill_tc.cuh"
 
-extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
+namespace {
+int chunk_prefill_impl(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
                                 const int64_t* context_lens, const int64_t* block_tables, int64_t bt_stride,
                                 int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer,
                                 int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, void* out,
                                 int64_t o_s0, int64_t o_s1, int num_seqs, int64_t total_q, int max_q_len,
-                                int num_q_heads, float scale, int dtype, int* control, void* stream) {
+                                int num_q_heads, float scale, int dtype, int* control, void* stream, int kv_dtype,
+                                float k_scale, float v_scale) {
   using namespace pa;
   if (num_seqs < 0 || total_q < 0 || max_q_len < 0 || num_kv_heads <= 0 || num_q_heads <= 0 ||
       num_q_heads % num_kv_heads != 0 || head_dim <= 0 || block_size <= 0 || num_blocks <= 0 || bt_width <= 0)
@@ -27,6 +29,8 @@ extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const
       k_pool_layer == nullptr || v_pool_layer == nullptr || out == nullptr)
     return PA_ERR_INVALID;
   if (dtype != PA_DTYPE_F32 && dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16) return PA_ERR_UNSUPPORTED;
+  const bool kv8 = kv_dtype == PA_DTYPE_FP8_E4M3;
+  if (kv8 && (!(k_scale > 0.f) || !(v_scale > 0.f) || isinf(k_scale) || isinf(v_scale))) return PA_ERR_INVALID;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int group = num_q_heads / num_kv_heads;
 
@@ -56,7 +60,8 @@ extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const
   a.scale = scale;
   a.dtype = dtype;
   a.control = control;
-  if (prefill_tc_supported(a)) return launch_prefill_tc(a, st);
+  // FP8 pools run on CUDA cores (the tensor-core kernel stages 16-bit K/V).
+  if (!kv8 && prefill_tc_supported(a)) return launch_prefill_tc(a, st);
 
   GenericParams g;
   g.q = q;
@@ -80,7 +85,8 @@ extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const
   g.D = head_dim;
   g.bs = block_size;
   g.group = group;
-  g.scale = scale;
+  g.scale = kv8 ? scale * k_scale : scale;
+  g.out_scale = kv8 ? v_scale : 1.f;
   // One split covering the whole context: the CTA walks it in chunks.
   const int chunk = generic_chunk_tokens();
   const int64_t max_tok = bt_width * (int64_t)block_size;
@@ -90,5 +96,30 @@ extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const
   g.part_o = nullptr;
   g.tickets = nullptr;
   g.status = nullptr;
-  return launch_attn_generic(g, dtype, 1, st);
+  return launch_attn_generic(g, dtype, 1, st, kv8 ? PA_DTYPE_FP8_E4M3 : dtype);
+}
+}  // namespace
+
+extern "C" int pa_chunk_prefill(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
+                                const int64_t* context_lens, const int64_t* block_tables, int64_t bt_stride,
+                                int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer,
+                                int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, void* out,
+                                int64_t o_s0, int64_t o_s1, int num_seqs, int64_t total_q, int max_q_len,
+                                int num_q_heads, float scale, int dtype, int* control, void* stream) {
+  return chunk_prefill_impl(q, q_s0, q_s1, cu_q_lens, context_lens, block_tables, bt_stride, bt_width, k_pool_layer,
+                            v_pool_layer, num_blocks, block_size, num_kv_heads, head_dim, out, o_s0, o_s1, num_seqs,
+                            total_q, max_q_len, num_q_heads, scale, dtype, control, stream, dtype, 1.f, 1.f);
+}
+
+extern "C" int pa_chunk_prefill_fp8(const void* q, int64_t q_s0, int64_t q_s1, const int64_t* cu_q_lens,
+                                    const int64_t* context_lens, const int64_t* block_tables, int64_t bt_stride,
+                                    int64_t bt_width, const void* k_pool_layer, const void* v_pool_layer,
+                                    int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, void* out,
+                                    int64_t o_s0, int64_t o_s1, int num_seqs, int64_t total_q, int max_q_len,
+                                    int num_q_heads, float scale, int dtype, float k_scale, float v_scale,
+                                    void* stream) {
+  return chunk_prefill_impl(q, q_s0, q_s1, cu_q_lens, context_lens, block_tables, bt_stride, bt_width, k_pool_layer,
+                            v_pool_layer, num_blocks, block_size, num_kv_heads, head_dim, out, o_s0, o_s1, num_seqs,
+                            total_q, max_q_len, num_q_heads, scale, dtype, nullptr, stream, PA_DTYPE_FP8_E4M3, k_scale,
+                            v_scale);
 }

@@ -25,8 +25,9 @@ int make_map_3d(CUtensorMap* map, int dtype, const void* base, uint64_t d0, uint
                 CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promotion) {
   EncodeTiledFn enc = get_encode_tiled();
   if (enc == nullptr) return PA_ERR_CUDA;
-  CUtensorMapDataType t =
-      dtype == PA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUtensorMapDataType t = dtype == PA_DTYPE_BF16        ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                          : dtype == PA_DTYPE_FP8_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   cuuint64_t dims[3] = {d0, d1, d2};
   cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
   cuuint32_t box[3] = {b0, b1, b2};

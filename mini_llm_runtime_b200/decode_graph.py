@@ -75,10 +75,15 @@ class PagedDecodeGraph:
         write_kv: bool = True,
         fuse_write: bool = True,
         early_inputs: bool = True,
+        query_dtype: torch.dtype | None = None,
     ):
         dev = _lib.require_cuda(cache.k_cache, what="PagedDecodeGraph")
-        if cache.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        if cache.dtype not in (torch.float16, torch.bfloat16, torch.float32, _lib.FP8_DTYPE):
             raise TypeError("unsupported cache dtype")
+        # q / new_k / new_v / outputs: the cache dtype, or BF16 over FP8 pools.
+        qdt = query_dtype or (torch.bfloat16 if cache.dtype == _lib.FP8_DTYPE else cache.dtype)
+        if cache.dtype != _lib.FP8_DTYPE and qdt != cache.dtype:
+            raise TypeError("query_dtype must be the cache dtype unless the pools are FP8")
         if num_q_heads % cache.num_kv_heads != 0:
             raise ValueError("num_query_heads must be divisible by num_kv_heads")
         self.cache = cache
@@ -99,7 +104,7 @@ class PagedDecodeGraph:
         self._flags = _lib.PA_DECODE_EARLY_INPUTS if early_inputs else 0
         self.scale = (1.0 / math.sqrt(cache.head_dim)) if scale is None else float(scale)
         L, B, H, D, HKV = len(self.layers), batch, num_q_heads, cache.head_dim, cache.num_kv_heads
-        dt = cache.dtype
+        dt = qdt
         # All of a step's inputs live in one byte buffer, the same layout on
         # the device and (pinned) on the host: the metadata, then one record
         # per layer [q | new_k | new_v], each 256-byte aligned.  A copy chunk
@@ -195,22 +200,34 @@ class PagedDecodeGraph:
             kp, vp = c.k_cache[layer], c.v_cache[layer]
             write = self.write_kv and not warm
             fused = write and self.fuse_write
+            fp8 = c.is_fp8
+            ks, vs = c.layer_scales(layer)
             if write and not fused:
-                st = lib.pa_kv_scatter(
-                    nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0),
-                    nv.stride(1), nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(),
-                    vp.data_ptr(), num_slots, HKV, D, self._code, stream)
+                if fp8:
+                    st = lib.pa_kv_scatter_fp8(
+                        nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0),
+                        nv.stride(1), nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(),
+                        vp.data_ptr(), num_slots, HKV, D, ks, vs, stream)
+                else:
+                    st = lib.pa_kv_scatter(
+                        nk.data_ptr(), nk.stride(0), nk.stride(1), nk.stride(2), nv.data_ptr(), nv.stride(0),
+                        nv.stride(1), nv.stride(2), self._code, self.slot_mapping.data_ptr(), 1, B, kp.data_ptr(),
+                        vp.data_ptr(), num_slots, HKV, D, self._code, stream)
                 _lib.check(st, "pa_kv_scatter")
             # After a separate scatter the decode reads pool rows that kernel
             # just wrote, so it waits before touching anything.
             flags = self._flags if (fused or not write) else 0
-            st = lib.pa_paged_decode_ex(
-                q.data_ptr(), q.stride(0), q.stride(1), nk.data_ptr() if fused else None,
-                nv.data_ptr() if fused else None, self.slot_mapping.data_ptr() if fused else None,
-                kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D, self.block_tables.data_ptr(),
-                self.block_tables.stride(0), self.width, self.context_lens.data_ptr(), o.data_ptr(), o.stride(0),
-                o.stride(1), B, H, self.scale, self._code, 0 if fused else self.partition_tokens, flags,
-                self.workspace.data_ptr(), self.workspace.numel(), stream)
+            args = (q.data_ptr(), q.stride(0), q.stride(1), nk.data_ptr() if fused else None,
+                    nv.data_ptr() if fused else None, self.slot_mapping.data_ptr() if fused else None,
+                    kp.data_ptr(), vp.data_ptr(), c.num_blocks, bs, HKV, D, self.block_tables.data_ptr(),
+                    self.block_tables.stride(0), self.width, self.context_lens.data_ptr(), o.data_ptr(), o.stride(0),
+                    o.stride(1), B, H, self.scale, self._code)
+            tail = (0 if fused else self.partition_tokens, flags, self.workspace.data_ptr(), self.workspace.numel(),
+                    stream)
+            if fp8:
+                st = lib.pa_paged_decode_fp8(*args, ks, vs, *tail)
+            else:
+                st = lib.pa_paged_decode_ex(*args, *tail)
             _lib.check(st, "pa_paged_decode_ex")
             if io and i in last_of_chunk:
                 a = last_of_chunk[i]
@@ -284,8 +301,8 @@ class PagedDecodeGraph:
         (main + combine kernel on the balanced path, one kernel otherwise)
         and, when the write is not fused into it, the KV scatter."""
         c = self.cache
-        balanced = (c.dtype in (torch.bfloat16, torch.float16) and c.head_dim in (64, 128) and c.block_size % 16 == 0
-                    and c.block_size <= 256 and self.batch <= 1024)
+        balanced = (self.out.dtype in (torch.bfloat16, torch.float16) and c.head_dim in (64, 128)
+                    and c.block_size % 16 == 0 and c.block_size <= 256 and self.batch <= 1024)
         per_layer = 2 if balanced else 1
         if self.write_kv and not (self.fuse_write and balanced):
             per_layer += 1

@@ -14,6 +14,8 @@ Differences from the reference that callers can observe:
 * BF16/F16 inputs keep scores and probabilities in FP32 inside the kernel
   (the reference rounds scores and probabilities to the input dtype,
   paged_attention.py:247-253), so results are closer to the FP32 reference.
+* the pools may be FP8 (torch.float8_e4m3fn, see PagedKVCache): pass the
+  layer's ``k_scale`` / ``v_scale`` keywords; q and the output keep q.dtype.
 """
 
 from __future__ import annotations
@@ -44,8 +46,9 @@ def _check_caches(k_cache: torch.Tensor, v_cache: torch.Tensor) -> None:
 
 
 def _pool_ok(k_cache: torch.Tensor, v_cache: torch.Tensor, dtype: torch.dtype) -> None:
-    if k_cache.dtype != dtype or v_cache.dtype != dtype:
-        raise TypeError("q, k_cache and v_cache must share one dtype")
+    fp8 = k_cache.dtype == _lib.FP8_DTYPE and v_cache.dtype == _lib.FP8_DTYPE
+    if not fp8 and (k_cache.dtype != dtype or v_cache.dtype != dtype):
+        raise TypeError("q, k_cache and v_cache must share one dtype (or the pools are FP8)")
     if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
         raise ValueError("k_cache and v_cache must be contiguous [num_blocks, block_size, Hkv, D] views")
 
@@ -66,6 +69,8 @@ def _decode_launch(
     out: torch.Tensor,
     partition_tokens: int,
     scale: float | None = None,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     dev = _lib.require_cuda(q, k_cache, v_cache, block_tables, seq_lens, out, what="paged decode")
     lib = _lib.load()
@@ -85,13 +90,22 @@ def _decode_launch(
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     with torch.cuda.device(dev):
-        st = lib.pa_paged_decode(
-            q.data_ptr(), q.stride(0), q.stride(1),
-            k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d,
-            block_tables.data_ptr(), block_tables.stride(0), width, seq_lens.data_ptr(),
-            out.data_ptr(), out.stride(0), out.stride(1), b, hq, float(scale), code,
-            int(partition_tokens), ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
-        )
+        if k_cache.dtype == _lib.FP8_DTYPE:
+            st = lib.pa_paged_decode_fp8(
+                q.data_ptr(), q.stride(0), q.stride(1), None, None, None,
+                k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d,
+                block_tables.data_ptr(), block_tables.stride(0), width, seq_lens.data_ptr(),
+                out.data_ptr(), out.stride(0), out.stride(1), b, hq, float(scale), code, float(k_scale),
+                float(v_scale), int(partition_tokens), 0, ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
+            )
+        else:
+            st = lib.pa_paged_decode(
+                q.data_ptr(), q.stride(0), q.stride(1),
+                k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d,
+                block_tables.data_ptr(), block_tables.stride(0), width, seq_lens.data_ptr(),
+                out.data_ptr(), out.stride(0), out.stride(1), b, hq, float(scale), code,
+                int(partition_tokens), ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
+            )
     _lib.check(st, "pa_paged_decode")
     _lib.after_launch(dev)
     return out
@@ -108,6 +122,9 @@ def paged_decode_with_kv_write(
     seq_lens: torch.Tensor,
     block_size: int,
     scale: float | None = None,
+    *,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """The decode step of Qwen2Attention.forward_decode_batch_with_cache
     (model/qwen2.py:608-621) in one fused launch: write the new token's K/V
@@ -136,8 +153,9 @@ def paged_decode_with_kv_write(
     dev = _lib.require_cuda(q, new_k, new_v, slot_mapping, k_cache, v_cache, block_tables, seq_lens,
                             what="paged_decode_with_kv_write")
     _pool_ok(k_cache, v_cache, q.dtype)
-    if new_k.dtype != q.dtype or new_v.dtype != q.dtype:
-        raise TypeError("new_k / new_v must have the KV cache dtype")
+    fp8 = k_cache.dtype == _lib.FP8_DTYPE
+    if new_k.dtype != q.dtype or new_v.dtype != q.dtype or (not fp8 and new_k.dtype != k_cache.dtype):
+        raise TypeError("new_k / new_v must have the dtype of q (and of the KV cache unless it is FP8)")
     lib = _lib.load()
     new_k, new_v = new_k.contiguous(), new_v.contiguous()
     slots = _as_long(slot_mapping, dev).contiguous()
@@ -157,12 +175,21 @@ def paged_decode_with_kv_write(
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     with torch.cuda.device(dev):
-        st = lib.pa_paged_decode_write(
-            q.data_ptr(), q.stride(0), q.stride(1), new_k.data_ptr(), new_v.data_ptr(), slots.data_ptr(),
-            k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d, block_tables.data_ptr(), block_tables.stride(0),
-            width, seq_lens.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), b, hq, float(scale), code,
-            ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
-        )
+        if fp8:
+            st = lib.pa_paged_decode_fp8(
+                q.data_ptr(), q.stride(0), q.stride(1), new_k.data_ptr(), new_v.data_ptr(), slots.data_ptr(),
+                k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d, block_tables.data_ptr(),
+                block_tables.stride(0), width, seq_lens.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), b,
+                hq, float(scale), code, float(k_scale), float(v_scale), 0, 0, ws.data_ptr(), ws.numel(),
+                _lib.stream_handle(dev),
+            )
+        else:
+            st = lib.pa_paged_decode_write(
+                q.data_ptr(), q.stride(0), q.stride(1), new_k.data_ptr(), new_v.data_ptr(), slots.data_ptr(),
+                k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d, block_tables.data_ptr(),
+                block_tables.stride(0), width, seq_lens.data_ptr(), out.data_ptr(), out.stride(0), out.stride(1), b,
+                hq, float(scale), code, ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
+            )
     _lib.check(st, "pa_paged_decode_write")
     _lib.after_launch(dev)
     return out
@@ -175,6 +202,9 @@ def paged_attention_decode_batch_parallel(
     block_tables: torch.Tensor,
     seq_lens: torch.Tensor,
     block_size: int,
+    *,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """Batched single-token decode: q [B, Hq, D] -> [B, Hq, D] (q.dtype).
 
@@ -203,7 +233,7 @@ def paged_attention_decode_batch_parallel(
     if block_tables.ndim != 2:
         raise ValueError("block_tables must have shape [B, max_num_blocks]")
     out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    return _decode_launch(q, k_cache, v_cache, block_tables, seq_lens, out, 0)
+    return _decode_launch(q, k_cache, v_cache, block_tables, seq_lens, out, 0, k_scale=k_scale, v_scale=v_scale)
 
 
 def paged_attention_decode_split_kv(
@@ -214,6 +244,9 @@ def paged_attention_decode_split_kv(
     seq_lens: torch.Tensor,
     block_size: int,
     partition_size: int = 512,
+    *,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """Split-KV decode with an LSE merge, batched.
 
@@ -253,7 +286,7 @@ def paged_attention_decode_split_kv(
     bt = _as_long(bt, q3.device)
     sl = _as_long(sl, q3.device)
     out = torch.empty_like(q3, memory_format=torch.contiguous_format)
-    _decode_launch(q3, k_cache, v_cache, bt, sl, out, int(partition_size))
+    _decode_launch(q3, k_cache, v_cache, bt, sl, out, int(partition_size), k_scale=k_scale, v_scale=v_scale)
     return out[0] if single else out
 
 
@@ -264,6 +297,9 @@ def paged_attention_decode(
     block_table: list[int],
     seq_len: int,
     block_size: int,
+    *,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """Single-sequence decode: q [Hq, D] -> [Hq, D].
 
@@ -292,7 +328,7 @@ def paged_attention_decode(
     sl = torch.tensor([seq_len], dtype=torch.long).to(q.device, non_blocking=True)
     q3 = q.unsqueeze(0)
     out = torch.empty_like(q3, memory_format=torch.contiguous_format)
-    _decode_launch(q3, k_cache, v_cache, bt.reshape(1, -1), sl, out, 0)
+    _decode_launch(q3, k_cache, v_cache, bt.reshape(1, -1), sl, out, 0, k_scale=k_scale, v_scale=v_scale)
     return out[0]
 
 
@@ -305,6 +341,8 @@ def _prefill_launch(
     v_cache: torch.Tensor,
     max_q_len: int,
     scale: float | None = None,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     dev = _lib.require_cuda(q, cu_q_lens, context_lens, block_tables, k_cache, v_cache, what="chunk prefill")
     lib = _lib.load()
@@ -317,14 +355,24 @@ def _prefill_launch(
     out = torch.empty((total_q, hq, d), dtype=q.dtype, device=q.device)
     if scale is None:
         scale = 1.0 / math.sqrt(d)
+    cu_q_lens, context_lens = cu_q_lens.contiguous(), context_lens.contiguous()
     with torch.cuda.device(dev):
-        st = lib.pa_chunk_prefill(
-            q.data_ptr(), q.stride(0), q.stride(1), cu_q_lens.contiguous().data_ptr(),
-            context_lens.contiguous().data_ptr(), block_tables.data_ptr(), block_tables.stride(0),
-            block_tables.shape[1], k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d,
-            out.data_ptr(), out.stride(0), out.stride(1), cu_q_lens.shape[0] - 1, total_q, int(max_q_len), hq,
-            float(scale), _lib.dtype_code(q.dtype), _lib.status_word(dev).data_ptr(), _lib.stream_handle(dev),
-        )
+        if k_cache.dtype == _lib.FP8_DTYPE:
+            st = lib.pa_chunk_prefill_fp8(
+                q.data_ptr(), q.stride(0), q.stride(1), cu_q_lens.data_ptr(), context_lens.data_ptr(),
+                block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], k_cache.data_ptr(),
+                v_cache.data_ptr(), nb, bs, hkv, d, out.data_ptr(), out.stride(0), out.stride(1),
+                cu_q_lens.shape[0] - 1, total_q, int(max_q_len), hq, float(scale), _lib.dtype_code(q.dtype),
+                float(k_scale), float(v_scale), _lib.stream_handle(dev),
+            )
+        else:
+            st = lib.pa_chunk_prefill(
+                q.data_ptr(), q.stride(0), q.stride(1), cu_q_lens.data_ptr(), context_lens.data_ptr(),
+                block_tables.data_ptr(), block_tables.stride(0), block_tables.shape[1], k_cache.data_ptr(),
+                v_cache.data_ptr(), nb, bs, hkv, d, out.data_ptr(), out.stride(0), out.stride(1),
+                cu_q_lens.shape[0] - 1, total_q, int(max_q_len), hq, float(scale), _lib.dtype_code(q.dtype),
+                _lib.status_word(dev).data_ptr(), _lib.stream_handle(dev),
+            )
     _lib.check(st, "pa_chunk_prefill")
     _lib.after_launch(dev)
     return out
@@ -339,6 +387,9 @@ def paged_attention_prefill_chunk_tiled(
     context_len: int,
     block_size: int,
     tile_size: int,
+    *,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """Causal chunk-prefill for one request: q [C, Hq, D] -> [C, Hq, D].
 
@@ -366,7 +417,7 @@ def paged_attention_prefill_chunk_tiled(
     if bt.shape[1] * block_size < context_len:
         raise ValueError("block_table does not contain enough blocks for context_len")
     meta = torch.tensor([0, q.shape[0], context_len], dtype=torch.long).to(dev, non_blocking=True)
-    return _prefill_launch(q, meta[:2], meta[2:], bt, k_cache, v_cache, q.shape[0])
+    return _prefill_launch(q, meta[:2], meta[2:], bt, k_cache, v_cache, q.shape[0], k_scale=k_scale, v_scale=v_scale)
 
 
 def paged_attention_prefill_varlen(
@@ -378,6 +429,9 @@ def paged_attention_prefill_varlen(
     v_cache: torch.Tensor,
     max_q_len: int,
     scale: float | None = None,
+    *,
+    k_scale: float = 1.0,
+    v_scale: float = 1.0,
 ) -> torch.Tensor:
     """Batched causal chunk-prefill over packed queries (ModelBatch layout).
 
@@ -403,7 +457,7 @@ def paged_attention_prefill_varlen(
     _pool_ok(k_cache, v_cache, q.dtype)
     return _prefill_launch(
         q, _as_long(cu_q_lens, q.device), _as_long(context_lens, q.device), _as_long(block_tables, q.device),
-        k_cache, v_cache, max_q_len, scale,
+        k_cache, v_cache, max_q_len, scale, k_scale, v_scale,
     )
 
 

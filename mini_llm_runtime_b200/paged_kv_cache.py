@@ -7,6 +7,12 @@ slot = block * block_size + offset), LIFO free list, per-sequence block
 tables and the same exceptions.  The block allocator is host bookkeeping and
 stays Python; ``write_slots`` — the batched KV-cache write on the hot path —
 launches the scatter kernel of libpagedattn.so.
+
+``dtype=torch.float8_e4m3fn`` stores the pools in FP8 (half the bytes decode
+streams; the reference has no FP8 pool): each layer has a K and a V scale
+(``k_scale`` / ``v_scale``: one float or one per layer), a stored element is
+``clamp(x / scale, -448, 448)`` rounded to nearest even, and the attention
+ops read it back as ``element * scale`` (pass ``*cache.layer_scales(l)``).
 """
 
 from __future__ import annotations
@@ -26,6 +32,8 @@ class PagedKVCache:
         head_dim: int,
         dtype: torch.dtype = torch.float16,
         device: torch.device | str = "cpu",
+        k_scale: float | list[float] = 1.0,
+        v_scale: float | list[float] = 1.0,
     ):
         self.num_layers = num_layers
         self.num_blocks = num_blocks
@@ -34,6 +42,10 @@ class PagedKVCache:
         self.head_dim = head_dim
         self.dtype = dtype
         self.device = torch.device(device)
+        self.k_scales = self._per_layer(k_scale, num_layers, "k_scale")
+        self.v_scales = self._per_layer(v_scale, num_layers, "v_scale")
+        if dtype != _lib.FP8_DTYPE and (any(s != 1.0 for s in self.k_scales) or any(s != 1.0 for s in self.v_scales)):
+            raise ValueError("k_scale / v_scale apply to FP8 pools only")
         shape = (num_layers, num_blocks, block_size, num_kv_heads, head_dim)
         self.k_cache = torch.empty(shape, dtype=dtype, device=device)
         self.v_cache = torch.empty_like(self.k_cache)
@@ -41,6 +53,23 @@ class PagedKVCache:
         self.free_blocks = list(range(num_blocks - 1, -1, -1))
         self.block_tables: dict[int, list[int]] = {}
         self.seq_lens: dict[int, int] = {}
+
+    @staticmethod
+    def _per_layer(scale, num_layers: int, name: str) -> list[float]:
+        vals = [float(scale)] * num_layers if isinstance(scale, (int, float)) else [float(s) for s in scale]
+        if len(vals) != num_layers:
+            raise ValueError(f"{name} must be one float or one per layer")
+        if not all(s > 0 and s != float("inf") for s in vals):
+            raise ValueError(f"{name} must be positive and finite")
+        return vals
+
+    @property
+    def is_fp8(self) -> bool:
+        return self.dtype == _lib.FP8_DTYPE
+
+    def layer_scales(self, layer_idx: int) -> tuple[float, float]:
+        """(k_scale, v_scale) of a layer (1.0 for 16/32-bit pools)."""
+        return self.k_scales[layer_idx], self.v_scales[layer_idx]
 
     # -- host-side allocator (paged_kv_cache.py:42-192) ---------------------
     def add_sequence(self, seq_id) -> None:
@@ -183,6 +212,23 @@ class PagedKVCache:
             return
         dev = _lib.require_cuda(self.k_cache, slot_mapping, k, v, what="PagedKVCache.write_slots")
         lib = _lib.load()
+        if self.is_fp8:
+            # Quantized in FP32: x / scale, saturated to +-448, nearest even.
+            if k.dtype != v.dtype:
+                k, v = k.float(), v.float()
+            layer_k, layer_v = self.k_cache[layer_idx], self.v_cache[layer_idx]
+            slot_mapping = slot_mapping.contiguous()
+            ks, vs = self.layer_scales(layer_idx)
+            with torch.cuda.device(dev):
+                st = lib.pa_kv_scatter_fp8(
+                    k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+                    v.data_ptr(), v.stride(0), v.stride(1), v.stride(2), _lib.dtype_code(k.dtype),
+                    slot_mapping.data_ptr(), int(slot_mapping.dtype == torch.int64), slot_mapping.numel(),
+                    layer_k.data_ptr(), layer_v.data_ptr(), self.num_blocks * self.block_size,
+                    self.num_kv_heads, self.head_dim, ks, vs, _lib.stream_handle(dev),
+                )
+            _lib.check(st, "pa_kv_scatter_fp8")
+            return
         if k.dtype != v.dtype:
             # Mixed sources: convert each exactly like the reference's `.to` (:246-247).
             k, v = k.to(self.dtype), v.to(self.dtype)

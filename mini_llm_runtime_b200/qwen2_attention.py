@@ -142,6 +142,19 @@ class Qwen2QKVProjection(nn.Module):
         return q, k, v
 
 
+def _is_fp8(kv_cache) -> bool:
+    return getattr(kv_cache, "is_fp8", False)
+
+
+def _scales(kv_cache, layer_idx: int) -> dict:
+    """The layer's FP8 pool scales as op keywords ({} for 16/32-bit pools and
+    for caches without scales, such as the reference's own PagedKVCache)."""
+    if not _is_fp8(kv_cache):
+        return {}
+    ks, vs = kv_cache.layer_scales(layer_idx)
+    return {"k_scale": ks, "v_scale": vs}
+
+
 class Qwen2Attention(nn.Module):
     """Drop-in for the reference's Qwen2Attention paged methods.
 
@@ -208,7 +221,8 @@ class Qwen2Attention(nn.Module):
         q, k, v = self.project(hidden_states, position_ids)
         kv_cache.write_slots(slot_mapping=slot_mapping, k=k.squeeze(1), v=v.squeeze(1), layer_idx=layer_idx)
         k_layer, v_layer = kv_cache.get_layer_cache(layer_idx)
-        out = paged_attention_decode(q[0, 0], k_layer, v_layer, block_table, context_len, kv_cache.block_size)
+        out = paged_attention_decode(q[0, 0], k_layer, v_layer, block_table, context_len, kv_cache.block_size,
+                                     **_scales(kv_cache, layer_idx))
         return self.o_proj(out.reshape(1, 1, self.hidden_size))
 
     # -- model/qwen2.py:542-622 ------------------------------------------------
@@ -236,7 +250,7 @@ class Qwen2Attention(nn.Module):
                 raise ValueError(f"{name} must be on the hidden_states device")
         if kv_cache.k_cache.device != hidden_states.device:
             raise ValueError("KV cache must be on the hidden_states device")
-        if kv_cache.dtype != hidden_states.dtype:
+        if kv_cache.dtype != hidden_states.dtype and not _is_fp8(kv_cache):
             raise ValueError("KV cache dtype must match hidden_states dtype")
         # One device->host copy of all metadata, then the reference's checks.
         w = block_tables.shape[1]
@@ -249,12 +263,13 @@ class Qwen2Attention(nn.Module):
         if new_token_blocks_private(lens_h, host[3 * batch:].reshape(batch, w), kv_cache.block_size):
             # KV write and decode in one launch (slots checked above).
             out = paged_decode_with_kv_write(q.squeeze(1), k.squeeze(1), v.squeeze(1), slot_mapping, k_layer,
-                                             v_layer, block_tables, context_lens, kv_cache.block_size)
+                                             v_layer, block_tables, context_lens, kv_cache.block_size,
+                                             **_scales(kv_cache, layer_idx))
         else:
             kv_cache.write_slots(slot_mapping=slot_mapping, k=k.squeeze(1), v=v.squeeze(1), layer_idx=layer_idx,
                                  validate=False)
             out = paged_attention_decode_batch_parallel(q.squeeze(1), k_layer, v_layer, block_tables, context_lens,
-                                                        kv_cache.block_size)
+                                                        kv_cache.block_size, **_scales(kv_cache, layer_idx))
         return self.o_proj(out.reshape(batch, 1, self.hidden_size))
 
     # -- model/qwen2.py:624-767 ------------------------------------------------
@@ -302,7 +317,7 @@ class Qwen2Attention(nn.Module):
         kv_cache.write_slots(slot_mapping=slot_mapping, k=k.squeeze(0), v=v.squeeze(0), layer_idx=layer_idx)
         k_layer, v_layer = kv_cache.get_layer_cache(layer_idx)
         out = paged_attention_prefill_chunk_tiled(q.squeeze(0), k_layer, v_layer, block_table, prefix_len,
-                                                  context_len, bs, tile_size)
+                                                  context_len, bs, tile_size, **_scales(kv_cache, layer_idx))
         return self.o_proj(out.reshape(1, chunk, self.hidden_size))
 
     # -- batched varlen chunk-prefill (no reference counterpart) --------------
@@ -354,5 +369,5 @@ class Qwen2Attention(nn.Module):
                              validate=False)
         max_q = int(chunks.max()) if nseq else 0
         out = paged_attention_prefill_varlen(q.squeeze(0), query_start_loc, context_lens, block_tables, k_layer,
-                                             v_layer, max_q)
+                                             v_layer, max_q, **_scales(kv_cache, layer_idx))
         return self.o_proj(out.reshape(1, total, self.hidden_size))

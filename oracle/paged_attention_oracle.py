@@ -58,6 +58,64 @@ def round_to_f16(x: np.ndarray) -> np.ndarray:
 
 
 # ---------------------------------------------------------------------------
+# FP8 (e4m3, "fn": no infinities, max finite 448) KV-pool elements
+# ---------------------------------------------------------------------------
+
+E4M3_MAX = 448.0
+
+
+def f32_to_e4m3_bits(x: np.ndarray) -> np.ndarray:
+    """float32 -> e4m3fn bit patterns (uint8): saturate to +-448, round to
+    nearest even; every NaN -> 0x7f.  For non-NaN inputs the same bytes as
+    ``torch.clamp(x, -448, 448).to(torch.float8_e4m3fn)`` (c10's
+    round-to-nearest-even cast; the clamp because torch's plain cast maps
+    overflow to NaN).  NaN signs are not kept: GPU arithmetic on a NaN (the
+    division by the scale) returns the canonical positive NaN.  The reference
+    has no FP8 pool; this is the storage format the FP8 PagedKVCache defines."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    sign = (np.signbit(x).astype(np.uint8)) << 7
+    a = np.minimum(np.abs(x), np.float32(E4M3_MAX)).astype(np.float32)
+    u = a.view(np.uint32).astype(np.int64)
+    exp = (u >> 23) - 127
+    out = np.zeros(x.shape, dtype=np.int64)
+    normal = exp >= -6
+    # Normal range: keep 3 mantissa bits, round to nearest even on the 20 dropped.
+    lsb = (u >> 20) & 1
+    r = (u + 0x7FFFF + lsb) >> 20  # (exponent << 3 | mantissa), float32 bias
+    out = np.where(normal, r - ((127 - 7) << 3), out)
+    # Subnormal range: multiples of 2^-9, nearest even (np.rint is RNE).
+    sub = np.rint(np.nan_to_num(a.astype(np.float64)) * 512.0).astype(np.int64)
+    out = np.where(normal, out, sub)
+    out = out.astype(np.uint8) | sign
+    nan = np.isnan(x)
+    if nan.any():
+        out = out.copy()
+        out[nan] = 0x7F
+    return out
+
+
+def e4m3_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    """e4m3fn bit patterns -> float32 (exact)."""
+    b = np.asarray(b, dtype=np.uint8).astype(np.int64)
+    s = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> 3) & 0xF
+    m = b & 0x7
+    val = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7.0))
+    val = np.where((e == 0xF) & (m == 0x7), np.nan, val)
+    return (s * val).astype(np.float32)
+
+
+def quantize_e4m3(x: np.ndarray, scale: float) -> np.ndarray:
+    """Stored FP8 byte of each element: e4m3(x / scale), the division in FP32."""
+    return f32_to_e4m3_bits(np.asarray(x, dtype=np.float32) / np.float32(scale))
+
+
+def dequantize_e4m3(bits: np.ndarray, scale: float) -> np.ndarray:
+    """What attention reads from an FP8 pool: element * scale (FP32)."""
+    return e4m3_bits_to_f32(bits) * np.float32(scale)
+
+
+# ---------------------------------------------------------------------------
 # KV-cache write
 # ---------------------------------------------------------------------------
 

@@ -25,9 +25,14 @@ TOL = dict(rtol=1e-2, atol=2e-2)
 HOST_BATCH = 16  # sequences gathered to the host at a time
 
 
-def _gather(pool: torch.Tensor, table_row: np.ndarray, need: int) -> np.ndarray:
+def _gather(pool: torch.Tensor, table_row: np.ndarray, need: int, scale: float = 1.0) -> np.ndarray:
+    """A sequence's blocks of a pool on the host in FP32 (FP8 pools: the
+    dequantized values, element * scale)."""
     idx = torch.as_tensor(np.ascontiguousarray(table_row[:need]), device=pool.device)
-    return pool.index_select(0, idx).float().cpu().numpy()
+    blocks = pool.index_select(0, idx)
+    if blocks.dtype == torch.float8_e4m3fn:
+        return O.dequantize_e4m3(blocks.view(torch.uint8).cpu().numpy(), scale)
+    return blocks.float().cpu().numpy()
 
 
 def oracle_case(inp: dict) -> np.ndarray:
@@ -60,13 +65,14 @@ def oracle_case(inp: dict) -> np.ndarray:
             batch = []
             for b in range(b0, min(b0 + HOST_BATCH, len(ctx))):
                 need = (int(ctx[b]) + bs - 1) // bs
-                batch.append((b, _gather(k, tables[b], need), _gather(v, tables[b], need)))
+                batch.append((b, _gather(k, tables[b], need, inp.get("k_scale", 1.0)),
+                              _gather(v, tables[b], need, inp.get("v_scale", 1.0))))
             list(ex.map(lambda a: run(*a), batch))
     return out
 
 
-@pytest.mark.parametrize("name", ["decode-config2", "split-config3", "prefill-config4", "decode-config5",
-                                  "prefill-config5"])
+@pytest.mark.parametrize("name", ["decode-config2", "decode-config2-fp8", "split-config3", "prefill-config4",
+                                  "decode-config5", "prefill-config5"])
 def test_bench_case_matches_oracle_at_full_size(cuda_device, name):
     build = bench.KERNEL_CASES[name][0]
     case = build(cuda_device, 1)
