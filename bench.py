@@ -314,6 +314,11 @@ def _case_config5_decode(device, layers):
     return _decode_case(device, layers, ctx, 28, 4, 128, 0, 15)
 
 
+def _case_config5_decode_fp8(device, layers):
+    ctx = np.random.default_rng(5).integers(256, 8193, size=256).astype(np.int64)
+    return _decode_case(device, layers, ctx, 28, 4, 128, 0, 15, fp8=True)
+
+
 def _case_config5_prefill(device, layers):
     prefix = np.random.default_rng(6).integers(0, 4097, size=4).astype(np.int64)
     return _prefill_case(device, layers, prefix, np.full(4, 1024, dtype=np.int64), 28, 4, 128, 16)
@@ -332,6 +337,9 @@ KERNEL_CASES = {
                         "config4: bf16 causal chunk-prefill, 16 seqs x 512 on prefix U[0,2048], 14/2, D64"),
     "decode-config5": (_case_config5_decode, "hbm", 2,
                        "config5 decode half: bf16 batched decode, B256, 28/4, D128, ctx U[256,8192]"),
+    "decode-config5-fp8": (_case_config5_decode_fp8, "hbm", 2,
+                           "config5 decode half over an FP8 (e4m3) KV pool: bf16 queries, B256, 28/4, D128, "
+                           "ctx U[256,8192]; bytes counted at 1 B per KV element"),
     "prefill-config5": (_case_config5_prefill, "tensor", 4,
                         "config5 prefill half: bf16 chunk-prefill, 4 x 1024 on prefix U[0,4096], 28/4, D128"),
 }
@@ -746,7 +754,8 @@ def main():
     # ---- secondary configs, one kernel at a time (same GPU, after the step) --
     secondary = {}
     if world == 1:
-        for name in ("split-config3", "prefill-config4", "decode-config5", "prefill-config5", "decode-config2-fp8"):
+        for name in ("split-config3", "prefill-config4", "decode-config5", "prefill-config5", "decode-config2-fp8",
+                     "decode-config5-fp8"):
             r = time_kernel_case(name, device)
             secondary[name] = {k: r[k] for k in ("workload", "us_per_launch", "achieved", "unit", "frac")}
             torch.cuda.empty_cache()
