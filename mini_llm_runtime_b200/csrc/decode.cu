@@ -65,11 +65,37 @@ __device__ __forceinline__ int row_head(int r, int group, int hn) {
   return r < hn ? r : -1;
 }
 
+// Two e4m3 values (low byte first) as an f16x2 MMA register (exact).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v & 0xffffu), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a 16 x 64-byte tile
+// written by TMA with 64-byte swizzle (chunk bits 4-5 ^= address bits 7-8).
+__device__ __forceinline__ uint32_t swz64(int row, int chunk) {
+  return static_cast<uint32_t>(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
+}
+
 // Online-softmax state of one warp for one piece of a segment: 16 MMA rows
 // of query heads, FP32 (m, l) per row in the log2 domain and the FP32 O
 // accumulator fragments.  Shared-memory stage layout: tile t = (kv * kColTiles
 // + ct) * PK + h holds 16 tokens x 64 dims of KV head h of the pack (SW128).
-template <typename T, int D, int PK>
+//
+// P8: the tiles hold e4m3 bytes (16 tokens x 64 bytes, 64-byte swizzle) and
+// feed the f16 MMAs straight from ldmatrix, converted in registers:
+//  * S = Q K^T: an ldmatrix lane receives 4 consecutive bytes (dims 4t..4t+3
+//    of a 16-dim k-step) of one token.  The k-step's dims are taken in the
+//    order that makes those the lane's B fragment (MMA k-positions 2t, 2t+1,
+//    2t+8, 2t+9 hold dims 4t .. 4t+3), and the Q fragments use the same
+//    order, which leaves every dot product unchanged.
+//  * O = P V: ldmatrix.trans of a 16-byte column block gives a lane bytes
+//    (token 2t: dims 2g, 2g+1; token 2t+1: dims 2g, 2g+1); one byte permute
+//    splits them into the B fragment of the even dims and of the odd dims, so
+//    accumulator tile 2c holds dims 16c + 2n and tile 2c + 1 dims 16c + 2n + 1
+//    — a lane's four values of a row are dims 16c + 4t .. + 3.
+// No dequantized copy is written to shared memory.
+template <typename T, int D, int PK, bool P8 = false>
 struct WarpState {
   static constexpr int kKK = D / 16;  // k-steps of S = Q K^T
   static constexpr int kDT = D / 8;   // n-tiles of O = P V
@@ -106,11 +132,12 @@ struct WarpState {
     const TQ* p1 = qb + (int64_t)(h0 + (e1 < 0 ? 0 : e1)) * q_s1;
 #pragma unroll
     for (int kk = 0; kk < kKK; ++kk) {
-      const int c = kk * 16 + cq;
+      // P8: k-positions 2t, 2t+1 / 2t+8, 2t+9 take dims 4t, 4t+1 / 4t+2, 4t+3.
+      const int c = kk * 16 + (P8 ? 4 * (lane & 3) : cq), c2 = c + (P8 ? 2 : 8);
       qa_out[kk][0] = e0 >= 0 ? q_pair(p0 + c) : 0u;
       qa_out[kk][1] = e1 >= 0 ? q_pair(p1 + c) : 0u;
-      qa_out[kk][2] = e0 >= 0 ? q_pair(p0 + c + 8) : 0u;
-      qa_out[kk][3] = e1 >= 0 ? q_pair(p1 + c + 8) : 0u;
+      qa_out[kk][2] = e0 >= 0 ? q_pair(p0 + c2) : 0u;
+      qa_out[kk][3] = e1 >= 0 ? q_pair(p1 + c2) : 0u;
     }
   }
 
@@ -133,13 +160,38 @@ struct WarpState {
   // sub-block u belong to the context.
   template <int NSUB>
   __device__ __forceinline__ void consume(const uint32_t* stage, const int* valid, float scale_log2, int lane) {
-    constexpr uint32_t kVOff = kColTiles * PK * kTileBytes;
+    constexpr uint32_t kT8 = kSub * 64;  // one e4m3 tile
+    constexpr uint32_t kVOff = kColTiles * PK * (P8 ? kT8 : kTileBytes);
     const int mi = lane >> 3, mr = lane & 7, cq = 2 * (lane & 3);
     float s[2 * NSUB][4];
 #pragma unroll
     for (int i = 0; i < 2 * NSUB; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+    // P8 ldmatrix.x4 rows: matrices 0 / 1 are tokens 0-7 / 8-15 of 16-byte
+    // chunk 2j, matrices 2 / 3 the same tokens of chunk 2j + 1.
+    const int tok8 = (mi & 1) * 8 + mr;
+    if constexpr (P8) {
 #pragma unroll
-    for (int kk = 0; kk < kKK; ++kk) {
+      for (int kp = 0; kp < kKK / 2; ++kp) {
+        const uint32_t off = (kp >> 1) * PK * kT8 + swz64(tok8, 2 * (kp & 1) + (mi >> 1));
+#pragma unroll
+        for (int h = 0; h < PK; ++h) {
+          uint32_t a0[4], a1[4];
+          head_rows(qa[2 * kp], h, a0);
+          head_rows(qa[2 * kp + 1], h, a1);
+#pragma unroll
+          for (int u = 0; u < NSUB; ++u) {
+            uint32_t r0, r1, r2, r3;
+            ldsm_x4(stage[u] + h * kT8 + off, r0, r1, r2, r3);
+            MmaOp<T>::run(s[2 * u], a0, e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r0 >> 16));
+            MmaOp<T>::run(s[2 * u + 1], a0, e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r1 >> 16));
+            MmaOp<T>::run(s[2 * u], a1, e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r2 >> 16));
+            MmaOp<T>::run(s[2 * u + 1], a1, e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r3 >> 16));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < (P8 ? 0 : kKK); ++kk) {
       const int ct = kk >> 2, kin = kk & 3;
       const int row = (mi >> 1) * 8 + mr;
       const int chunk = 2 * kin + (mi & 1);
@@ -215,8 +267,29 @@ struct WarpState {
       for (int h = 0; h < PK; ++h) {
         uint32_t ap[4];
         head_rows(pa, h, ap);
+        if constexpr (P8) {
 #pragma unroll
-        for (int dt = 0; dt < kDT; dt += 2) {
+          for (int jp = 0; jp < kDT / 4; ++jp) {
+            uint32_t r0, r1, r2, r3;
+            ldsm_x4_t(stage[u] + kVOff + ((jp >> 1) * PK + h) * kT8 + swz64(tok8, 2 * (jp & 1) + (mi >> 1)), r0, r1,
+                      r2, r3);
+            if (partial) {  // r0 / r2: tokens cq, cq+1; r1 / r3: 8+cq, 9+cq
+              r0 &= mlo;
+              r2 &= mlo;
+              r1 &= mhi;
+              r3 &= mhi;
+            }
+            // Low half: the even dim of both tokens; high half: the odd dim.
+            const uint32_t e0 = __byte_perm(r0, 0u, 0x3120), e1 = __byte_perm(r1, 0u, 0x3120);
+            const uint32_t e2 = __byte_perm(r2, 0u, 0x3120), e3 = __byte_perm(r3, 0u, 0x3120);
+            MmaOp<T>::run(o[4 * jp], ap, e4m3x2_to_f16x2(e0), e4m3x2_to_f16x2(e1));
+            MmaOp<T>::run(o[4 * jp + 1], ap, e4m3x2_to_f16x2(e0 >> 16), e4m3x2_to_f16x2(e1 >> 16));
+            MmaOp<T>::run(o[4 * jp + 2], ap, e4m3x2_to_f16x2(e2), e4m3x2_to_f16x2(e3));
+            MmaOp<T>::run(o[4 * jp + 3], ap, e4m3x2_to_f16x2(e2 >> 16), e4m3x2_to_f16x2(e3 >> 16));
+          }
+        }
+#pragma unroll
+        for (int dt = 0; dt < (P8 ? 0 : kDT); dt += 2) {
           const int dtt = dt + (mi >> 1);
           const int row = (mi & 1) * 8 + mr;
           uint32_t v0, v1, v2, v3;
@@ -255,8 +328,16 @@ struct WarpState {
       a1[0] = m1;
       a1[1] = l1;
     }
+    if constexpr (P8) {  // dims 16c + 4t .. + 3 = tiles (2c, 2c+1) x (c0, c1)
 #pragma unroll
-    for (int dt = 0; dt < kDT; ++dt) {
+      for (int c = 0; c < kDT / 2; ++c) {
+        const int f = 4 + c * 16 + 2 * cq;
+        *reinterpret_cast<float4*>(a0 + f) = make_float4(o[2 * c][0], o[2 * c + 1][0], o[2 * c][1], o[2 * c + 1][1]);
+        *reinterpret_cast<float4*>(a1 + f) = make_float4(o[2 * c][2], o[2 * c + 1][2], o[2 * c][3], o[2 * c + 1][3]);
+      }
+    }
+#pragma unroll
+    for (int dt = 0; dt < (P8 ? 0 : kDT); ++dt) {
       const int c = 4 + dt * 8 + cq;
       *reinterpret_cast<float2*>(a0 + c) = make_float2(o[dt][0], o[dt][1]);
       *reinterpret_cast<float2*>(a1 + c) = make_float2(o[dt][2], o[dt][3]);
@@ -271,8 +352,24 @@ struct WarpState {
     const int r0 = lane >> 2, cq = 2 * (lane & 3);
     const int e0 = row_head<PK>(r0, group, hn), e1 = row_head<PK>(r0 + 8, group, hn);
     const float i0 = out_scale / l0, i1 = out_scale / l1;
+    if constexpr (P8) {
 #pragma unroll
-    for (int dt = 0; dt < kDT; ++dt) {
+      for (int c = 0; c < kDT / 2; ++c) {
+        const int d = c * 16 + 2 * cq;
+        if (e0 >= 0) {
+          TO* dst = ob + (int64_t)(h0 + e0) * o_s1 + d;
+          *reinterpret_cast<uint32_t*>(dst) = MmaOp<TO>::pack(o[2 * c][0] * i0, o[2 * c + 1][0] * i0);
+          *reinterpret_cast<uint32_t*>(dst + 2) = MmaOp<TO>::pack(o[2 * c][1] * i0, o[2 * c + 1][1] * i0);
+        }
+        if (e1 >= 0) {
+          TO* dst = ob + (int64_t)(h0 + e1) * o_s1 + d;
+          *reinterpret_cast<uint32_t*>(dst) = MmaOp<TO>::pack(o[2 * c][2] * i1, o[2 * c + 1][2] * i1);
+          *reinterpret_cast<uint32_t*>(dst + 2) = MmaOp<TO>::pack(o[2 * c][3] * i1, o[2 * c + 1][3] * i1);
+        }
+      }
+    }
+#pragma unroll
+    for (int dt = 0; dt < (P8 ? 0 : kDT); ++dt) {
       if (e0 >= 0)
         *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e0) * o_s1 + dt * 8 + cq) =
             MmaOp<TO>::pack(o[dt][0] * i0, o[dt][1] * i0);
@@ -391,71 +488,36 @@ __device__ __forceinline__ void seg_heads(const FlatParams& p, int segx, int& kv
   }
 }
 
-// KV8: FP8 pools.  A ring stage then holds the FP8 tiles (16 tokens x 64
-// bytes, 1 KB, unswizzled), and each warp has a dequant buffer of NSUB
-// sub-blocks in the 16-bit swizzled layout the MMA loads read.
+// KV8: FP8 pools.  A ring stage then holds e4m3 tiles (16 tokens x 64
+// bytes, 1 KB, 64-byte swizzle) that the MMA fragments are loaded from.
 template <int D, int PK, int NW, int STAGES, int NSUB = 1, bool KV8 = false>
 struct FlatCfg {
   static constexpr int kColTiles = D / 64;
   static constexpr int kTile8 = kSub * 64;  // one FP8 tile: 16 tokens x 64 bytes
-  static constexpr int kStage16 = 2 * kColTiles * PK * kTileBytes;  // K + V of one sub-block, 16-bit
-  static constexpr int kStageBytes = KV8 ? 2 * kColTiles * PK * kTile8 : kStage16;
+  static constexpr int kStageBytes = 2 * kColTiles * PK * (KV8 ? kTile8 : kTileBytes);  // K + V of a sub-block
   static constexpr int kRingBytes = NW * STAGES * kStageBytes;
-  static constexpr int kDeqBytes = KV8 ? NW * NSUB * kStage16 : 0;  // per-warp dequant buffers
   static constexpr int kRec = D + 4;  // record floats per row
   static constexpr int kRecBytes = 16 * kRec * 4;
   static constexpr int kStagingBytes = NW * kRecBytes;  // first-piece record per warp
   static constexpr int kPrefixBytes = (kFlatMaxBatch + 1) * 4;
-  static constexpr int kOffDeq = kRingBytes;
-  static constexpr int kOffStaging = kOffDeq + kDeqBytes;
+  static constexpr int kOffStaging = kRingBytes;
   static constexpr int kOffPrefix = kOffStaging + kStagingBytes;
   static constexpr int kOffBars = kOffPrefix + ((kPrefixBytes + 15) & ~15);
   static constexpr size_t kSmem = 1024 + kOffBars + NW * STAGES * 8 + 64;
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
-  // At the end a warp's ring (its dequant buffer with FP8) holds its last-piece record.
-  static constexpr int kRecAreaBytes = KV8 ? NSUB * kStage16 : STAGES * kStageBytes;
-  static_assert(kRecAreaBytes >= kRecBytes, "a warp's ring holds its last-piece record at the end");
-  __device__ __forceinline__ static int rec_area(int warp) {
-    return KV8 ? kOffDeq + warp * NSUB * kStage16 : warp * STAGES * kStageBytes;
-  }
+  static_assert(STAGES * kStageBytes >= kRecBytes, "a warp's ring holds its last-piece record at the end");
+  __device__ __forceinline__ static int rec_area(int warp) { return warp * STAGES * kStageBytes; }
 };
 
-// FP8 stage -> 16-bit tiles in the swizzled layout of the BF16/F16 path
-// (f16 values: exact for every e4m3 value).  Lane i converts 16-byte chunks
-// i, i + 32, ...: chunk c of FP8 tile t is row (c % 64) / 4, bytes
-// 16 * (c % 4) .. + 16, and becomes two 16-byte chunks of 16-bit tile t.
-template <int NTILES>
-__device__ __forceinline__ void dequant_fp8_stage(const uint8_t* src, uint8_t* dst, int lane) {
-#pragma unroll
-  for (int k = 0; k < NTILES * 64 / 32; ++k) {
-    const int c = lane + 32 * k;
-    const int t = c >> 6, r = (c & 63) >> 2, cc = c & 3;
-    const int4 raw = *reinterpret_cast<const int4*>(src + t * kSub * 64 + r * 64 + cc * 16);
-    const uint32_t w[4] = {static_cast<uint32_t>(raw.x), static_cast<uint32_t>(raw.y), static_cast<uint32_t>(raw.z),
-                           static_cast<uint32_t>(raw.w)};
-    uint32_t h[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] & 0xffffu), __NV_E4M3);
-      const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] >> 16), __NV_E4M3);
-      h[2 * i] = static_cast<uint32_t>(lo.x) | (static_cast<uint32_t>(lo.y) << 16);
-      h[2 * i + 1] = static_cast<uint32_t>(hi.x) | (static_cast<uint32_t>(hi.y) << 16);
-    }
-    uint8_t* d = dst + t * kTileBytes + r * kTileRowBytes;
-    *reinterpret_cast<int4*>(d + (((2 * cc) ^ (r & 7)) << 4)) = make_int4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<int4*>(d + (((2 * cc + 1) ^ (r & 7)) << 4)) = make_int4(h[4], h[5], h[6], h[7]);
-  }
-}
-
-// TQ: query / output elements.  KV8: FP8 pools, MMAs in f16 on the
-// dequantized tiles (T is the MMA element type).
+// TQ: query / output elements.  KV8: FP8 pools, f16 MMAs on fragments
+// converted from the e4m3 tiles in registers (T is the MMA element type).
 template <typename TQ, int D, int PK, int NW, int STAGES, int NSUB, int CTAS, bool KV8>
 __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                                                    const __grid_constant__ CUtensorMap tmap_v,
                                                                    FlatParams p) {
   using T = typename std::conditional<KV8, __half, TQ>::type;
   using C = FlatCfg<D, PK, NW, STAGES, NSUB, KV8>;
-  using WS = WarpState<T, D, PK>;
+  using WS = WarpState<T, D, PK, KV8>;
   constexpr int kTileX = KV8 ? C::kTile8 : kTileBytes;  // bytes of one staged tile
   static_assert(STAGES >= NSUB, "a consume step takes NSUB staged sub-blocks");
   constexpr int NT = NW * 32;
@@ -625,13 +687,7 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
           const int j = jc + u;
           const int stage = j % STAGES;
           if (ok) ok = mbar_wait(&wbar[stage], (j / STAGES) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
-          // The tiles the MMAs read: the stage itself, or (FP8) its dequantized copy.
           uint8_t* tiles = ring + stage * C::kStageBytes;
-          if (KV8) {
-            uint8_t* dq = smem + C::kOffDeq + (warp * NSUB + u) * C::kStage16;
-            if (ok) dequant_fp8_stage<2 * C::kColTiles * PK>(tiles, dq, lane);
-            tiles = dq;
-          }
           stg[u] = smem_u32(tiles);
           const int64_t sub = lo + j - pc.start;
           valid[u] = static_cast<int>(min((int64_t)kSub, ctx - sub * kSub));
@@ -652,52 +708,41 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
               const int64_t src = ((int64_t)b * p.Hkv + kvh0 + h) * D + ct * 64 + cc * 8;
               const int4 val =
                   __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const TQ*>(kv ? p.new_v : p.new_k) + src));
-              uint8_t* dst = tiles + t * kTileBytes + r * 128 + ((cc ^ (r & 7)) << 4);
               const int64_t pool_el = (slot * p.Hkv + kvh0 + h) * D + ct * 64 + cc * 8;
               if (KV8) {
                 // Quantize as the FP8 scatter does (x / scale, saturated,
-                // nearest even), store the bytes, and patch their f16 values.
+                // nearest even); the 8 bytes go to the staged tile (half of
+                // a swizzled 16-byte chunk) and to the pools.
                 const TQ* e = reinterpret_cast<const TQ*>(&val);
                 const float sc = kv ? p.v_scale : p.k_scale;
-                uint32_t f8[2] = {0u, 0u}, hv[4];
+                uint32_t f8[2] = {0u, 0u};
 #pragma unroll
-                for (int k2 = 0; k2 < 8; k2 += 2) {
-                  const uint32_t b0 = __nv_cvt_float_to_fp8(__fdiv_rn(Elem<TQ>::to_f32(e[k2]), sc), __NV_SATFINITE,
-                                                            __NV_E4M3);
-                  const uint32_t b1 = __nv_cvt_float_to_fp8(__fdiv_rn(Elem<TQ>::to_f32(e[k2 + 1]), sc),
-                                                            __NV_SATFINITE, __NV_E4M3);
-                  f8[k2 >> 2] |= (b0 | (b1 << 8)) << (8 * (k2 & 3));
-                  const __half2_raw hh =
-                      __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(b0 | (b1 << 8)), __NV_E4M3);
-                  hv[k2 >> 1] = static_cast<uint32_t>(hh.x) | (static_cast<uint32_t>(hh.y) << 16);
+                for (int k2 = 0; k2 < 8; ++k2) {
+                  const uint32_t b8 =
+                      __nv_cvt_float_to_fp8(__fdiv_rn(Elem<TQ>::to_f32(e[k2]), sc), __NV_SATFINITE, __NV_E4M3);
+                  f8[k2 >> 2] |= b8 << (8 * (k2 & 3));
                 }
-                *reinterpret_cast<int4*>(dst) = make_int4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<uint2*>(tiles + t * C::kTile8 + swz64(r, cc >> 1) + (cc & 1) * 8) =
+                    make_uint2(f8[0], f8[1]);
                 if (store_pool && slot >= 0 && slot < p.num_slots)
                   *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(kv ? p.v_pool : p.k_pool) + pool_el) =
                       make_uint2(f8[0], f8[1]);
               } else {
-                *reinterpret_cast<int4*>(dst) = val;
+                *reinterpret_cast<int4*>(tiles + t * kTileBytes + r * 128 + ((cc ^ (r & 7)) << 4)) = val;
                 if (store_pool && slot >= 0 && slot < p.num_slots)
                   *reinterpret_cast<int4*>(reinterpret_cast<TQ*>(kv ? p.v_pool : p.k_pool) + pool_el) = val;
               }
             }
-            if (!KV8) fence_proxy_async_smem();  // before the stage is refilled by TMA
+            fence_proxy_async_smem();  // before the stage is refilled by TMA
             __syncwarp();
           }
         }
       }
       if (!ok) break;
-      if (KV8) {
-        // The FP8 stages are free once dequantized: refill them before the MMAs.
-        __syncwarp();
-        for (int u = 0; u < n; ++u)
-          if (issued < nj) issue(issued++);
-      }
       if (n == NSUB) ws.template consume<NSUB>(stg, valid, p.scale_log2, lane);
       else ws.template consume<1>(stg, valid, p.scale_log2, lane);
       __syncwarp();
-      if (!KV8)
-        for (int u = 0; u < n; ++u)
+      for (int u = 0; u < n; ++u)
           if (issued < nj) issue(issued++);
       jc += n;
     }
@@ -727,8 +772,8 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
     for (int j = jc; j < issued; ++j) mbar_wait(&wbar[j % STAGES], (j / STAGES) & 1, p.status, PA_DEVICE_TIMEOUT_TMA);
     first_sid = last_sid = -1;
   }
-  // This warp's copies have all landed: its ring (or dequant buffer) is free
-  // for the last-piece record.
+  // This warp's copies have all landed: its ring is free for the last-piece
+  // record.
   if (last_sid >= 0) ws.store(reinterpret_cast<float*>(smem + C::rec_area(warp)), lane);
   if (lane == 0) {
     ent_seg[2 * warp] = first_sid;
@@ -1108,7 +1153,10 @@ int current_device() {
 // merge tail overlap the other's streaming and, with PDL, the next kernel's
 // CTAs move in as soon as one exits.  A stage is one sub-block of every head
 // of the pack: 8 KB (D = 64, PK = 2) to 16 KB (D = 128, PK = 2).
-// FP8 pools halve a stage, so they take one more ring stage.
+// FP8 pools halve a stage: at D = 64 they take one more ring stage, at
+// D = 128 twice the warps (8 per SM), since an FP8 byte costs twice the MMA
+// and conversion work of a BF16 byte and one warp per scheduler cannot hide
+// that latency.
 template <int D, int PK, bool KV8 = false> struct FlatShape;
 template <> struct FlatShape<64, 2> { static constexpr int NW = 4, ST = 2, NSUB = 1; };
 template <> struct FlatShape<64, 1> { static constexpr int NW = 4, ST = 4, NSUB = 2; };
@@ -1116,8 +1164,8 @@ template <> struct FlatShape<128, 2> { static constexpr int NW = 2, ST = 2, NSUB
 template <> struct FlatShape<128, 1> { static constexpr int NW = 2, ST = 4, NSUB = 2; };
 template <> struct FlatShape<64, 2, true> { static constexpr int NW = 4, ST = 3, NSUB = 1; };
 template <> struct FlatShape<64, 1, true> { static constexpr int NW = 4, ST = 4, NSUB = 2; };
-template <> struct FlatShape<128, 2, true> { static constexpr int NW = 2, ST = 3, NSUB = 1; };
-template <> struct FlatShape<128, 1, true> { static constexpr int NW = 2, ST = 4, NSUB = 2; };
+template <> struct FlatShape<128, 2, true> { static constexpr int NW = 4, ST = 2, NSUB = 1; };
+template <> struct FlatShape<128, 1, true> { static constexpr int NW = 4, ST = 4, NSUB = 2; };
 constexpr int kFlatCtasPerSm = 2;
 constexpr int kSplitNW = 4, kSplitST = 4;
 
@@ -1401,9 +1449,9 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
     const int map_dtype = kv8 ? PA_DTYPE_FP8_E4M3 : dtype;
     // Rows of one KV head are 128 B (64 B with FP8) with a Hkv-row stride; a
     // wider L2 promotion would drag the other heads' rows in ahead of their
-    // readers.  FP8 tiles land unswizzled (64-byte rows); the warp rewrites
-    // them as swizzled f16 tiles.
-    const CUtensorMapSwizzle swz_mode = kv8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B;
+    // readers.  The swizzle spans one row, so the MMA fragment loads (8 rows
+    // of one 16-byte column) hit distinct banks.
+    const CUtensorMapSwizzle swz_mode = kv8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
     const CUtensorMapL2promotion l2p = kv8 ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B : CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
     if (make_map_3d(&tk, map_dtype, k_pool_layer, head_dim, num_kv_heads, slots, s1b, s2b, 64, 1, 16, swz_mode,
                     l2p) != PA_OK ||
