@@ -215,6 +215,15 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "r"(addr));
 }
 
+// Transpose of an 8x8 matrix of 16-bit elements held in MMA fragment layout
+// (lane l: row l / 4, columns 2 (l % 4), +1): lane l receives row l / 4 of
+// the transpose.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 template <typename T> struct MmaOp;
 template <> struct MmaOp<__nv_bfloat16> {
   __device__ __forceinline__ static void run(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {

@@ -5,23 +5,23 @@
 // split-KV pair (kernels/triton/paged_attention.py:528-700 stage 1,
 // :1530-1618 merge) to a ragged batch.
 //
-// Fast path (F16/BF16, head_dim 64 or 128, block_size % 16 == 0, batch <=
-// 1024) — HBM-bound: decode_flat_kernel, then decode_combine_kernel.
+// Fast path (F16/BF16 queries over F16/BF16 or FP8 e4m3 pools, head_dim 64
+// or 128, block_size % 16 == 0, batch <= 1024) — HBM-bound:
+// decode_flat_kernel, then decode_combine_kernel.
 //  * The batch's KV is one index space of 16-token sub-blocks ordered by
 //    (sequence, KV-head pack, position).  Each CTA owns an equal contiguous
 //    range of it and each warp an equal part of its CTA's range, so every SM
 //    streams the same number of bytes whatever the context lengths.
 //  * A warp streams its sub-blocks through its own TMA ring (3-D boxes
-//    {64 dims, 1 head, 16 tokens}, 128-byte swizzle, mbarrier completion),
-//    looking the physical block of each sub-block up in a lane-cached slice
-//    of the block table.
-//  * Scores S = Q K^T and O += P V use mma.sync m16n8k16 with FP32
-//    accumulators.  When a GQA group has at most 8 query heads and the KV
-//    heads pair up, one warp serves two KV heads at once: rows 0-7 of the MMA
-//    hold the first head's query group and rows 8-15 the second's, and each
-//    head's K/V enter the MMA with the other half of the A operand zeroed.
-//    Every row of the tile then carries a real query head, so the online
-//    softmax does no work on padding rows.
+//    {64 dims, 1 head, 16 tokens}, 128-byte swizzle — 64-byte for FP8 —
+//    mbarrier completion), looking the physical block of each sub-block up
+//    in a lane-cached slice of the block table.
+//  * S^T = K Q^T and O^T += V^T P^T use mma.sync m16n8k16 with FP32
+//    accumulators, tokens / head dims as M and 8 query heads as N.  When a
+//    GQA group has at most 8 query heads and the KV heads pair up, one warp
+//    serves two KV heads at once, one 8-column tile each, so a group of 7
+//    fills 7 of 8 columns of every MMA.  FP8 tiles feed the MMAs through
+//    in-register e4m3 -> f16 conversion of the ldmatrix fragments.
 //  * Online softmax in FP32, log2 domain (scores pre-multiplied by
 //    scale * log2(e), exp2f).
 //  * A segment (one sequence x one KV-head pack) that lies inside one warp's
@@ -53,9 +53,10 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {  // byte offset in
   return static_cast<uint32_t>(row * kTileRowBytes + ((chunk ^ (row & 7)) << 4));
 }
 
-// Query head (relative to the piece's first head) of MMA row r, or -1 for a
-// padding row.  PK = 2: rows 0-7 serve the first KV head's group, rows 8-15
-// the second's (group <= 8).  PK = 1: rows 0..hn-1 are consecutive heads.
+// Query head (relative to the piece's first head) of record row r (column r
+// % 8 of column tile r / 8), or -1 for padding.  PK = 2: rows 0-7 serve the
+// first KV head's group, rows 8-15 the second's (group <= 8).  PK = 1: rows
+// 0..hn-1 are consecutive heads.
 template <int PK>
 __device__ __forceinline__ int row_head(int r, int group, int hn) {
   if (PK == 2) {
@@ -77,201 +78,204 @@ __device__ __forceinline__ uint32_t swz64(int row, int chunk) {
   return static_cast<uint32_t>(row * 64 + ((chunk ^ ((row >> 1) & 3)) << 4));
 }
 
-// Online-softmax state of one warp for one piece of a segment: 16 MMA rows
-// of query heads, FP32 (m, l) per row in the log2 domain and the FP32 O
-// accumulator fragments.  Shared-memory stage layout: tile t = (kv * kColTiles
-// + ct) * PK + h holds 16 tokens x 64 dims of KV head h of the pack (SW128).
+// Two adjacent query elements as one MMA register (converted when the MMA
+// type differs from the query type: FP8 pools run the MMAs in f16).
+template <typename T, typename TQ>
+__device__ __forceinline__ uint32_t q_pair(const TQ* p) {
+  if constexpr (std::is_same<T, TQ>::value) {
+    return load_pair_u32(p);
+  } else {
+    return MmaOp<T>::pack(Elem<TQ>::to_f32(p[0]), Elem<TQ>::to_f32(p[1]));
+  }
+}
+
+// Online-softmax state of one warp for one piece of a segment, in the
+// transposed orientation S^T = K Q^T, O^T = V^T P^T: 16 tokens (S^T) or 16
+// head dims (O^T) are the MMA's M and 8 query heads its N.  A warp serves two
+// column tiles j of 8 query heads: PK = 2, the GQA group of KV head j of the
+// pack (<= 8 heads); PK = 1, heads 8j .. 8j + 7 of a <= 16-head tile (both
+// read the same K/V, so one set of fragments serves both tiles).  A group of
+// 7 heads then fills 7 of 8 columns of every MMA.  Column n of tile j is
+// record row 8j + n.  FP32 (m, l) per column in the log2 domain.
 //
-// P8: the tiles hold e4m3 bytes (16 tokens x 64 bytes, 64-byte swizzle) and
-// feed the f16 MMAs straight from ldmatrix, converted in registers:
-//  * S = Q K^T: an ldmatrix lane receives 4 consecutive bytes (dims 4t..4t+3
-//    of a 16-dim k-step) of one token.  The k-step's dims are taken in the
-//    order that makes those the lane's B fragment (MMA k-positions 2t, 2t+1,
-//    2t+8, 2t+9 hold dims 4t .. 4t+3), and the Q fragments use the same
-//    order, which leaves every dot product unchanged.
-//  * O = P V: ldmatrix.trans of a 16-byte column block gives a lane bytes
+// Shared-memory stage layout: tile t = (kv * kColTiles + ct) * PK + h holds
+// 16 tokens x 64 dims of KV head h of the pack — 16-bit elements with
+// 128-byte swizzle, or (P8) e4m3 bytes with 64-byte swizzle.
+//  * S^T: A fragments are K rows straight from ldmatrix, B fragments Q^T.
+//    P8: an ldmatrix lane receives 4 consecutive bytes (dims 4t .. 4t+3 of a
+//    16-dim k-step) of one token; the k-step's dims are taken in the order
+//    that makes those its A fragment (k-positions 2t, 2t+1, 2t+8, 2t+9 hold
+//    dims 4t .. 4t+3), and the Q^T fragments use the same order, which leaves
+//    every dot product unchanged.  The bytes are converted to f16 (exact) in
+//    registers; no dequantized copy is written.
+//  * P^T: the exponentiated S^T fragments, packed to 16 bits, become B
+//    fragments (tokens 2t, 2t+1 of column g) by one movmatrix per 8x8 block.
+//  * O^T: A fragments are V^T from ldmatrix.trans.  16-bit pools: rows g /
+//    g + 8 of an m-tile are its dims g / g + 8.  P8: a lane receives bytes
 //    (token 2t: dims 2g, 2g+1; token 2t+1: dims 2g, 2g+1); one byte permute
-//    splits them into the B fragment of the even dims and of the odd dims, so
-//    accumulator tile 2c holds dims 16c + 2n and tile 2c + 1 dims 16c + 2n + 1
-//    — a lane's four values of a row are dims 16c + 4t .. + 3.
-// No dequantized copy is written to shared memory.
+//    splits them into dim 2g (row g) and dim 2g + 1 (row g + 8).
+// Per lane, accumulator element e of m-tile c of tile j holds column
+// 2t + (e & 1) and dim 16c + (P8 ? 2g + (e >> 1) : g + 8 (e >> 1)).
 template <typename T, int D, int PK, bool P8 = false>
 struct WarpState {
-  static constexpr int kKK = D / 16;  // k-steps of S = Q K^T
-  static constexpr int kDT = D / 8;   // n-tiles of O = P V
+  static constexpr int kKK = D / 16;  // k-steps of S^T; m-tiles of O^T
   static constexpr int kColTiles = D / 64;
-  uint32_t qa[kKK][4];
-  float m0, m1, l0, l1;
-  float o[kDT][4];
+  uint32_t qa[kKK][4];  // [kk][2j + i]: B fragment i of Q^T, column tile j
+  float m[2][2], l[2][2];  // [j][column 2t + c]
+  float o[2][kKK][4];
 
   __device__ __forceinline__ void reset() {
-    m0 = m1 = -INFINITY;
-    l0 = l1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < kDT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  }
-
-  // Two adjacent query elements as one MMA register (converted when the MMA
-  // type differs from the query type: FP8 pools run the MMAs in f16).
-  template <typename TQ>
-  __device__ __forceinline__ static uint32_t q_pair(const TQ* p) {
-    if constexpr (std::is_same<TQ, T>::value) {
-      return load_pair_u32(p);
-    } else {
-      return MmaOp<T>::pack(Elem<TQ>::to_f32(p[0]), Elem<TQ>::to_f32(p[1]));
+    for (int j = 0; j < 2; ++j) {
+      m[j][0] = m[j][1] = -INFINITY;
+      l[j][0] = l[j][1] = 0.f;
+#pragma unroll
+      for (int c = 0; c < kKK; ++c) o[j][c][0] = o[j][c][1] = o[j][c][2] = o[j][c][3] = 0.f;
     }
   }
 
-  // A fragments of Q for rows r0 = lane/4 and r1 = r0 + 8 (zeros for padding).
   template <typename TQ>
   __device__ __forceinline__ static void load_q(uint32_t (&qa_out)[kKK][4], const TQ* qb, int64_t q_s1, int h0,
                                                 int group, int hn, int lane) {
-    const int r0 = lane >> 2, cq = 2 * (lane & 3);
-    const int e0 = row_head<PK>(r0, group, hn), e1 = row_head<PK>(r0 + 8, group, hn);
-    const TQ* p0 = qb + (int64_t)(h0 + (e0 < 0 ? 0 : e0)) * q_s1;
-    const TQ* p1 = qb + (int64_t)(h0 + (e1 < 0 ? 0 : e1)) * q_s1;
+    const int g = lane >> 2, t = lane & 3;
 #pragma unroll
-    for (int kk = 0; kk < kKK; ++kk) {
-      // P8: k-positions 2t, 2t+1 / 2t+8, 2t+9 take dims 4t, 4t+1 / 4t+2, 4t+3.
-      const int c = kk * 16 + (P8 ? 4 * (lane & 3) : cq), c2 = c + (P8 ? 2 : 8);
-      qa_out[kk][0] = e0 >= 0 ? q_pair(p0 + c) : 0u;
-      qa_out[kk][1] = e1 >= 0 ? q_pair(p1 + c) : 0u;
-      qa_out[kk][2] = e0 >= 0 ? q_pair(p0 + c2) : 0u;
-      qa_out[kk][3] = e1 >= 0 ? q_pair(p1 + c2) : 0u;
+    for (int j = 0; j < 2; ++j) {
+      const int e = row_head<PK>(8 * j + g, group, hn);
+      const TQ* p = qb + (int64_t)(h0 + (e < 0 ? 0 : e)) * q_s1;
+#pragma unroll
+      for (int kk = 0; kk < kKK; ++kk) {
+        // P8: k-positions 2t, 2t+1 / 2t+8, 2t+9 take dims 4t, 4t+1 / 4t+2, 4t+3.
+        const int c = kk * 16 + (P8 ? 4 * t : 2 * t), c2 = c + (P8 ? 2 : 8);
+        qa_out[kk][2 * j] = e >= 0 ? q_pair<T, TQ>(p + c) : 0u;
+        qa_out[kk][2 * j + 1] = e >= 0 ? q_pair<T, TQ>(p + c2) : 0u;
+      }
     }
   }
 
-  // A operand of head h of the pack: PK = 2 keeps only that head's rows.
-  __device__ __forceinline__ static void head_rows(const uint32_t* a, int h, uint32_t* out) {
-    if (PK == 1) {
-      out[0] = a[0];
-      out[1] = a[1];
-      out[2] = a[2];
-      out[3] = a[3];
-    } else {
-      out[0] = h == 0 ? a[0] : 0u;
-      out[1] = h == 0 ? 0u : a[1];
-      out[2] = h == 0 ? a[2] : 0u;
-      out[3] = h == 0 ? 0u : a[3];
-    }
-  }
+  // Column tiles served by KV head h of the pack: PK = 2, tile h; PK = 1, both.
+  static constexpr int kTilesPerHead = PK == 2 ? 1 : 2;
 
-  // NSUB 16-token sub-blocks staged at stage[u]; the first valid[u] tokens of
-  // sub-block u belong to the context.
   template <int NSUB>
   __device__ __forceinline__ void consume(const uint32_t* stage, const int* valid, float scale_log2, int lane) {
-    constexpr uint32_t kT8 = kSub * 64;  // one e4m3 tile
-    constexpr uint32_t kVOff = kColTiles * PK * (P8 ? kT8 : kTileBytes);
-    const int mi = lane >> 3, mr = lane & 7, cq = 2 * (lane & 3);
-    float s[2 * NSUB][4];
-#pragma unroll
-    for (int i = 0; i < 2 * NSUB; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-    // P8 ldmatrix.x4 rows: matrices 0 / 1 are tokens 0-7 / 8-15 of 16-byte
-    // chunk 2j, matrices 2 / 3 the same tokens of chunk 2j + 1.
-    const int tok8 = (mi & 1) * 8 + mr;
-    if constexpr (P8) {
-#pragma unroll
-      for (int kp = 0; kp < kKK / 2; ++kp) {
-        const uint32_t off = (kp >> 1) * PK * kT8 + swz64(tok8, 2 * (kp & 1) + (mi >> 1));
-#pragma unroll
-        for (int h = 0; h < PK; ++h) {
-          uint32_t a0[4], a1[4];
-          head_rows(qa[2 * kp], h, a0);
-          head_rows(qa[2 * kp + 1], h, a1);
-#pragma unroll
-          for (int u = 0; u < NSUB; ++u) {
-            uint32_t r0, r1, r2, r3;
-            ldsm_x4(stage[u] + h * kT8 + off, r0, r1, r2, r3);
-            MmaOp<T>::run(s[2 * u], a0, e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r0 >> 16));
-            MmaOp<T>::run(s[2 * u + 1], a0, e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r1 >> 16));
-            MmaOp<T>::run(s[2 * u], a1, e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r2 >> 16));
-            MmaOp<T>::run(s[2 * u + 1], a1, e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r3 >> 16));
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int kk = 0; kk < (P8 ? 0 : kKK); ++kk) {
-      const int ct = kk >> 2, kin = kk & 3;
-      const int row = (mi >> 1) * 8 + mr;
-      const int chunk = 2 * kin + (mi & 1);
-#pragma unroll
-      for (int h = 0; h < PK; ++h) {
-        uint32_t a[4];
-        head_rows(qa[kk], h, a);
-#pragma unroll
-        for (int u = 0; u < NSUB; ++u) {
-          uint32_t b00, b01, b10, b11;
-          ldsm_x4(stage[u] + (ct * PK + h) * kTileBytes + swz(row, chunk), b00, b01, b10, b11);
-          MmaOp<T>::run(s[2 * u], a, b00, b01);
-          MmaOp<T>::run(s[2 * u + 1], a, b10, b11);
-        }
-      }
-    }
+    constexpr uint32_t kTile = P8 ? kSub * 64 : kTileBytes;
+    constexpr uint32_t kVOff = kColTiles * PK * kTile;
+    const int mi = lane >> 3, mr = lane & 7, g = lane >> 2, cq = 2 * (lane & 3);
+    float s[NSUB][2][4];
 #pragma unroll
     for (int u = 0; u < NSUB; ++u)
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int j = 0; j < 2; ++j) s[u][j][0] = s[u][j][1] = s[u][j][2] = s[u][j][3] = 0.f;
+    // ---- S^T = K Q^T ----
+#pragma unroll
+    for (int u = 0; u < NSUB; ++u)
+#pragma unroll
+      for (int h = 0; h < PK; ++h) {
+        if constexpr (P8) {
+          // Matrices 0 / 1: tokens 0-7 / 8-15 of 16-byte chunk 2k'; 2 / 3: of chunk 2k' + 1.
+          const int tok = (mi & 1) * 8 + mr;
+#pragma unroll
+          for (int kp = 0; kp < kKK / 2; ++kp) {
+            uint32_t r0, r1, r2, r3;
+            ldsm_x4(stage[u] + ((kp >> 1) * PK + h) * kTile + swz64(tok, 2 * (kp & 1) + (mi >> 1)), r0, r1, r2, r3);
+            const uint32_t a[4] = {e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
+                                   e4m3x2_to_f16x2(r1 >> 16)};
+            const uint32_t b[4] = {e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r2 >> 16),
+                                   e4m3x2_to_f16x2(r3 >> 16)};
+#pragma unroll
+            for (int jj = 0; jj < kTilesPerHead; ++jj) {
+              const int j = PK == 2 ? h : jj;
+              MmaOp<T>::run(s[u][j], a, qa[2 * kp][2 * j], qa[2 * kp][2 * j + 1]);
+              MmaOp<T>::run(s[u][j], b, qa[2 * kp + 1][2 * j], qa[2 * kp + 1][2 * j + 1]);
+            }
+          }
+        } else {
+          // Matrices: (tokens 0-7, dims 0-7), (8-15, 0-7), (0-7, 8-15), (8-15, 8-15) of the k-step.
+          const int tok = (mi & 1) * 8 + mr;
+#pragma unroll
+          for (int kk = 0; kk < kKK; ++kk) {
+            uint32_t a[4];
+            ldsm_x4(stage[u] + ((kk >> 2) * PK + h) * kTile + swz(tok, 2 * (kk & 3) + (mi >> 1)), a[0], a[1], a[2],
+                    a[3]);
+#pragma unroll
+            for (int jj = 0; jj < kTilesPerHead; ++jj) {
+              const int j = PK == 2 ? h : jj;
+              MmaOp<T>::run(s[u][j], a, qa[kk][2 * j], qa[kk][2 * j + 1]);
+            }
+          }
+        }
+      }
+    // ---- online softmax over the columns (query heads) ----
+    // Elements 0, 1: token g, columns cq, cq+1; elements 2, 3: token g + 8.
+#pragma unroll
+    for (int u = 0; u < NSUB; ++u)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int tok = nt * 8 + cq + (e & 1);
-          s[2 * u + nt][e] = tok < valid[u] ? s[2 * u + nt][e] * scale_log2 : -INFINITY;
+          const int tok = g + 8 * (e >> 1);
+          s[u][j][e] = tok < valid[u] ? s[u][j][e] * scale_log2 : -INFINITY;
         }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
+    float mn[2][2], al[2][2];
 #pragma unroll
-    for (int i = 0; i < 2 * NSUB; ++i) {
-      mx0 = fmaxf(mx0, fmaxf(s[i][0], s[i][1]));
-      mx1 = fmaxf(mx1, fmaxf(s[i][2], s[i][3]));
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-    const float a0 = exp2f(m0 - mn0), a1 = exp2f(m1 - mn1);
-    float sum0 = 0.f, sum1 = 0.f;
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-    for (int i = 0; i < 2 * NSUB; ++i) {
-      s[i][0] = exp2f(s[i][0] - mn0);
-      s[i][1] = exp2f(s[i][1] - mn0);
-      s[i][2] = exp2f(s[i][2] - mn1);
-      s[i][3] = exp2f(s[i][3] - mn1);
-      sum0 += s[i][0] + s[i][1];
-      sum1 += s[i][2] + s[i][3];
-    }
-    l0 = l0 * a0 + sum0;
-    l1 = l1 * a1 + sum1;
-    m0 = mn0;
-    m1 = mn1;
+      for (int c = 0; c < 2; ++c) {
+        float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kDT; ++i) {
-      o[i][0] *= a0;
-      o[i][1] *= a0;
-      o[i][2] *= a1;
-      o[i][3] *= a1;
+        for (int u = 0; u < NSUB; ++u) mx = fmaxf(mx, fmaxf(s[u][j][c], s[u][j][c + 2]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        mn[j][c] = fmaxf(m[j][c], mx);
+        al[j][c] = exp2f(m[j][c] - mn[j][c]);
+        m[j][c] = mn[j][c];
+      }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+      for (int u = 0; u < NSUB; ++u) {
+        s[u][j][0] = exp2f(s[u][j][0] - mn[j][0]);
+        s[u][j][1] = exp2f(s[u][j][1] - mn[j][1]);
+        s[u][j][2] = exp2f(s[u][j][2] - mn[j][0]);
+        s[u][j][3] = exp2f(s[u][j][3] - mn[j][1]);
+        sum0 += s[u][j][0] + s[u][j][2];
+        sum1 += s[u][j][1] + s[u][j][3];
+      }
+      l[j][0] = l[j][0] * al[j][0] + sum0;
+      l[j][1] = l[j][1] * al[j][1] + sum1;
+#pragma unroll
+      for (int c = 0; c < kKK; ++c) {
+        o[j][c][0] *= al[j][0];
+        o[j][c][1] *= al[j][1];
+        o[j][c][2] *= al[j][0];
+        o[j][c][3] *= al[j][1];
+      }
     }
+    // ---- O^T += V^T P^T ----
 #pragma unroll
     for (int u = 0; u < NSUB; ++u) {
-      uint32_t pa[4];
-      pa[0] = MmaOp<T>::pack(s[2 * u][0], s[2 * u][1]);
-      pa[1] = MmaOp<T>::pack(s[2 * u][2], s[2 * u][3]);
-      pa[2] = MmaOp<T>::pack(s[2 * u + 1][0], s[2 * u + 1][1]);
-      pa[3] = MmaOp<T>::pack(s[2 * u + 1][2], s[2 * u + 1][3]);
+      uint32_t pb[2][2];  // B fragments of P^T: tokens 2t, 2t+1 (0) / 2t+8, 2t+9 (1) of column g
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        pb[j][0] = movmatrix_t(MmaOp<T>::pack(s[u][j][0], s[u][j][1]));
+        pb[j][1] = movmatrix_t(MmaOp<T>::pack(s[u][j][2], s[u][j][3]));
+      }
       const int vu = valid[u];
       const bool partial = vu < kSub;
-      // v0/v2 hold tokens cq, cq+1; v1/v3 hold tokens 8+cq, 9+cq.  Tokens past
-      // the context are zeroed so stale / NaN slots cannot reach the sum.
+      // A registers of tokens cq, cq+1 (low / high half) and 8+cq, 9+cq:
+      // tokens past the context are zeroed so stale / NaN slots cannot
+      // reach the sum.
       const uint32_t mlo = (cq < vu ? 0x0000ffffu : 0u) | (cq + 1 < vu ? 0xffff0000u : 0u);
       const uint32_t mhi = (cq + 8 < vu ? 0x0000ffffu : 0u) | (cq + 9 < vu ? 0xffff0000u : 0u);
 #pragma unroll
       for (int h = 0; h < PK; ++h) {
-        uint32_t ap[4];
-        head_rows(pa, h, ap);
         if constexpr (P8) {
+          const int tok = (mi & 1) * 8 + mr;
 #pragma unroll
-          for (int jp = 0; jp < kDT / 4; ++jp) {
+          for (int jp = 0; jp < kKK / 2; ++jp) {
             uint32_t r0, r1, r2, r3;
-            ldsm_x4_t(stage[u] + kVOff + ((jp >> 1) * PK + h) * kT8 + swz64(tok8, 2 * (jp & 1) + (mi >> 1)), r0, r1,
+            ldsm_x4_t(stage[u] + kVOff + ((jp >> 1) * PK + h) * kTile + swz64(tok, 2 * (jp & 1) + (mi >> 1)), r0, r1,
                       r2, r3);
             if (partial) {  // r0 / r2: tokens cq, cq+1; r1 / r3: 8+cq, 9+cq
               r0 &= mlo;
@@ -279,68 +283,84 @@ struct WarpState {
               r1 &= mhi;
               r3 &= mhi;
             }
-            // Low half: the even dim of both tokens; high half: the odd dim.
+            // Low half: dim 2g of both tokens (row g); high half: dim 2g+1 (row g+8).
             const uint32_t e0 = __byte_perm(r0, 0u, 0x3120), e1 = __byte_perm(r1, 0u, 0x3120);
             const uint32_t e2 = __byte_perm(r2, 0u, 0x3120), e3 = __byte_perm(r3, 0u, 0x3120);
-            MmaOp<T>::run(o[4 * jp], ap, e4m3x2_to_f16x2(e0), e4m3x2_to_f16x2(e1));
-            MmaOp<T>::run(o[4 * jp + 1], ap, e4m3x2_to_f16x2(e0 >> 16), e4m3x2_to_f16x2(e1 >> 16));
-            MmaOp<T>::run(o[4 * jp + 2], ap, e4m3x2_to_f16x2(e2), e4m3x2_to_f16x2(e3));
-            MmaOp<T>::run(o[4 * jp + 3], ap, e4m3x2_to_f16x2(e2 >> 16), e4m3x2_to_f16x2(e3 >> 16));
-          }
-        }
+            const uint32_t a[4] = {e4m3x2_to_f16x2(e0), e4m3x2_to_f16x2(e0 >> 16), e4m3x2_to_f16x2(e1),
+                                   e4m3x2_to_f16x2(e1 >> 16)};
+            const uint32_t b[4] = {e4m3x2_to_f16x2(e2), e4m3x2_to_f16x2(e2 >> 16), e4m3x2_to_f16x2(e3),
+                                   e4m3x2_to_f16x2(e3 >> 16)};
 #pragma unroll
-        for (int dt = 0; dt < (P8 ? 0 : kDT); dt += 2) {
-          const int dtt = dt + (mi >> 1);
-          const int row = (mi & 1) * 8 + mr;
-          uint32_t v0, v1, v2, v3;
-          ldsm_x4_t(stage[u] + kVOff + ((dtt >> 3) * PK + h) * kTileBytes + swz(row, dtt & 7), v0, v1, v2, v3);
-          if (partial) {
-            v0 &= mlo;
-            v2 &= mlo;
-            v1 &= mhi;
-            v3 &= mhi;
+            for (int jj = 0; jj < kTilesPerHead; ++jj) {
+              const int j = PK == 2 ? h : jj;
+              MmaOp<T>::run(o[j][2 * jp], a, pb[j][0], pb[j][1]);
+              MmaOp<T>::run(o[j][2 * jp + 1], b, pb[j][0], pb[j][1]);
+            }
           }
-          MmaOp<T>::run(o[dt], ap, v0, v1);
-          MmaOp<T>::run(o[dt + 1], ap, v2, v3);
+        } else {
+          // Matrices: (tokens 0-7, dims 0-7), (0-7, 8-15), (8-15, 0-7), (8-15, 8-15) of the m-tile.
+          const int tok = (mi >> 1) * 8 + mr;
+#pragma unroll
+          for (int c = 0; c < kKK; ++c) {
+            uint32_t a[4];
+            ldsm_x4_t(stage[u] + kVOff + ((c >> 2) * PK + h) * kTile + swz(tok, 2 * (c & 3) + (mi & 1)), a[0], a[1],
+                      a[2], a[3]);
+            if (partial) {
+              a[0] &= mlo;
+              a[1] &= mlo;
+              a[2] &= mhi;
+              a[3] &= mhi;
+            }
+#pragma unroll
+            for (int jj = 0; jj < kTilesPerHead; ++jj) {
+              const int j = PK == 2 ? h : jj;
+              MmaOp<T>::run(o[j][c], a, pb[j][0], pb[j][1]);
+            }
+          }
         }
       }
     }
   }
 
-  // Sum the row sums over the 4 lanes of a quad (rows are spread that way).
+  // Sum the column sums over the 8 lanes of a column (tokens are spread that way).
   __device__ __forceinline__ void reduce_l() {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        l[j][c] += __shfl_xor_sync(0xffffffffu, l[j][c], 4);
+        l[j][c] += __shfl_xor_sync(0xffffffffu, l[j][c], 8);
+        l[j][c] += __shfl_xor_sync(0xffffffffu, l[j][c], 16);
+      }
   }
 
-  // Rows [0, 16) as records of kRec floats: {m, l, -, -, O[0..D)} (O starts
-  // 16-byte aligned so merges read it with float4 loads).  Call reduce_l first.
+  // Columns as records of kRec floats: {m, l, -, -, O[0..D)} at row 8j + n.
+  // Call reduce_l first.
   static constexpr int kRec = D + 4;
   __device__ __forceinline__ void store(float* area, int lane) const {
-    const int r0 = lane >> 2, r1 = r0 + 8, cq = 2 * (lane & 3);
-    float* a0 = area + r0 * kRec;
-    float* a1 = area + r1 * kRec;
-    if ((lane & 3) == 0) {
-      a0[0] = m0;
-      a0[1] = l0;
-      a1[0] = m1;
-      a1[1] = l1;
-    }
-    if constexpr (P8) {  // dims 16c + 4t .. + 3 = tiles (2c, 2c+1) x (c0, c1)
+    const int g = lane >> 2, cq = 2 * (lane & 3);
 #pragma unroll
-      for (int c = 0; c < kDT / 2; ++c) {
-        const int f = 4 + c * 16 + 2 * cq;
-        *reinterpret_cast<float4*>(a0 + f) = make_float4(o[2 * c][0], o[2 * c + 1][0], o[2 * c][1], o[2 * c + 1][1]);
-        *reinterpret_cast<float4*>(a1 + f) = make_float4(o[2 * c][2], o[2 * c + 1][2], o[2 * c][3], o[2 * c + 1][3]);
+    for (int j = 0; j < 2; ++j) {
+      float* r0 = area + (8 * j + cq) * kRec;
+      float* r1 = r0 + kRec;
+      if (g == 0) {
+        r0[0] = m[j][0];
+        r0[1] = l[j][0];
+        r1[0] = m[j][1];
+        r1[1] = l[j][1];
       }
-    }
 #pragma unroll
-    for (int dt = 0; dt < (P8 ? 0 : kDT); ++dt) {
-      const int c = 4 + dt * 8 + cq;
-      *reinterpret_cast<float2*>(a0 + c) = make_float2(o[dt][0], o[dt][1]);
-      *reinterpret_cast<float2*>(a1 + c) = make_float2(o[dt][2], o[dt][3]);
+      for (int c = 0; c < kKK; ++c) {
+        if constexpr (P8) {
+          *reinterpret_cast<float2*>(r0 + 4 + 16 * c + 2 * g) = make_float2(o[j][c][0], o[j][c][2]);
+          *reinterpret_cast<float2*>(r1 + 4 + 16 * c + 2 * g) = make_float2(o[j][c][1], o[j][c][3]);
+        } else {
+          r0[4 + 16 * c + g] = o[j][c][0];
+          r1[4 + 16 * c + g] = o[j][c][1];
+          r0[4 + 16 * c + 8 + g] = o[j][c][2];
+          r1[4 + 16 * c + 8 + g] = o[j][c][3];
+        }
+      }
     }
   }
 
@@ -349,33 +369,37 @@ struct WarpState {
   template <typename TO>
   __device__ __forceinline__ void store_out(TO* ob, int64_t o_s1, int h0, int group, int hn, int lane,
                                             float out_scale) const {
-    const int r0 = lane >> 2, cq = 2 * (lane & 3);
-    const int e0 = row_head<PK>(r0, group, hn), e1 = row_head<PK>(r0 + 8, group, hn);
-    const float i0 = out_scale / l0, i1 = out_scale / l1;
-    if constexpr (P8) {
+    const int g = lane >> 2, cq = 2 * (lane & 3);
 #pragma unroll
-      for (int c = 0; c < kDT / 2; ++c) {
-        const int d = c * 16 + 2 * cq;
-        if (e0 >= 0) {
-          TO* dst = ob + (int64_t)(h0 + e0) * o_s1 + d;
-          *reinterpret_cast<uint32_t*>(dst) = MmaOp<TO>::pack(o[2 * c][0] * i0, o[2 * c + 1][0] * i0);
-          *reinterpret_cast<uint32_t*>(dst + 2) = MmaOp<TO>::pack(o[2 * c][1] * i0, o[2 * c + 1][1] * i0);
+    for (int j = 0; j < 2; ++j) {
+      const float i0 = out_scale / l[j][0], i1 = out_scale / l[j][1];
+      if constexpr (P8) {
+        // Lane: dims 16c + 2g, +1 of columns cq and cq + 1.
+        const int e0 = row_head<PK>(8 * j + cq, group, hn), e1 = row_head<PK>(8 * j + cq + 1, group, hn);
+#pragma unroll
+        for (int c = 0; c < kKK; ++c) {
+          if (e0 >= 0)
+            *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e0) * o_s1 + 16 * c + 2 * g) =
+                MmaOp<TO>::pack(o[j][c][0] * i0, o[j][c][2] * i0);
+          if (e1 >= 0)
+            *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e1) * o_s1 + 16 * c + 2 * g) =
+                MmaOp<TO>::pack(o[j][c][1] * i1, o[j][c][3] * i1);
         }
-        if (e1 >= 0) {
-          TO* dst = ob + (int64_t)(h0 + e1) * o_s1 + d;
-          *reinterpret_cast<uint32_t*>(dst) = MmaOp<TO>::pack(o[2 * c][2] * i1, o[2 * c + 1][2] * i1);
-          *reinterpret_cast<uint32_t*>(dst + 2) = MmaOp<TO>::pack(o[2 * c][3] * i1, o[2 * c + 1][3] * i1);
+      } else {
+        // Lane: dims 16c + g and 16c + 8 + g of columns cq, cq + 1; one
+        // movmatrix per 8x8 block gives it dims 16c (+8) + cq, +1 of column g.
+        const int e = row_head<PK>(8 * j + g, group, hn);
+        TO* dst = ob + (int64_t)(h0 + (e < 0 ? 0 : e)) * o_s1 + cq;
+#pragma unroll
+        for (int c = 0; c < kKK; ++c) {
+          const uint32_t lo = movmatrix_t(MmaOp<TO>::pack(o[j][c][0] * i0, o[j][c][1] * i1));
+          const uint32_t hi = movmatrix_t(MmaOp<TO>::pack(o[j][c][2] * i0, o[j][c][3] * i1));
+          if (e >= 0) {
+            *reinterpret_cast<uint32_t*>(dst + 16 * c) = lo;
+            *reinterpret_cast<uint32_t*>(dst + 16 * c + 8) = hi;
+          }
         }
       }
-    }
-#pragma unroll
-    for (int dt = 0; dt < (P8 ? 0 : kDT); ++dt) {
-      if (e0 >= 0)
-        *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e0) * o_s1 + dt * 8 + cq) =
-            MmaOp<TO>::pack(o[dt][0] * i0, o[dt][1] * i0);
-      if (e1 >= 0)
-        *reinterpret_cast<uint32_t*>(ob + (int64_t)(h0 + e1) * o_s1 + dt * 8 + cq) =
-            MmaOp<TO>::pack(o[dt][2] * i1, o[dt][3] * i1);
     }
   }
 };

@@ -293,3 +293,19 @@ def test_fused_kv_write_matches_scatter_then_decode(cuda_device, dtype, d, hq, h
     q_np, _, _, tab_np, ctx_np = case["np"]
     exp = O.decode_batch(q_np, k2.float().cpu().numpy(), v2.float().cpu().numpy(), tab_np, ctx_np, bs)
     check(out, exp, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv,d", [(14, 2, 64), (28, 4, 128), (40, 2, 64)], ids=["gqa7", "gqa7x4", "gqa20"])
+def test_decode_batches_above_the_balanced_limit(cuda_device, dtype, hq, hkv, d):
+    """More than 1024 sequences: one CTA per (sequence, head tile,
+    partition) with a last-ticket merge instead of the balanced kernel."""
+    rng = np.random.default_rng(hq * 3 + d)
+    ctx = rng.integers(1, 160, size=1100).tolist()
+    ctx[7], ctx[1000] = 1500, 16
+    case = make_decode_case(ctx, hq, hkv, d, 16, dtype, cuda_device, seed=hq + d)
+    out = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+    check(out, oracle_decode(case), dtype)
+    split = paged_attention_decode_split_kv(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16,
+                                            partition_size=256)
+    check(split, oracle_decode(case), dtype)
