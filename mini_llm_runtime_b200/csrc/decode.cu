@@ -66,10 +66,14 @@ __device__ __forceinline__ int row_head(int r, int group, int hn) {
   return r < hn ? r : -1;
 }
 
-// Two e4m3 values (low byte first) as an f16x2 MMA register (exact).
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
-  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v & 0xffffu), __NV_E4M3);
-  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+// Four e4m3 values (bytes 0..3) as two f16x2 MMA registers (exact): lo =
+// bytes 0, 1 and hi = bytes 2, 3, low byte in the low half.  The 32-bit
+// register is split into its 16-bit halves in place, so no mask or shift
+// precedes the conversions.
+__device__ __forceinline__ void e4m3x4_to_f16x2(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
 }
 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a 16 x 64-byte tile
@@ -177,10 +181,11 @@ struct WarpState {
           for (int kp = 0; kp < kKK / 2; ++kp) {
             uint32_t r0, r1, r2, r3;
             ldsm_x4(stage[u] + ((kp >> 1) * PK + h) * kTile + swz64(tok, 2 * (kp & 1) + (mi >> 1)), r0, r1, r2, r3);
-            const uint32_t a[4] = {e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
-                                   e4m3x2_to_f16x2(r1 >> 16)};
-            const uint32_t b[4] = {e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r2 >> 16),
-                                   e4m3x2_to_f16x2(r3 >> 16)};
+            uint32_t a[4], b[4];
+            e4m3x4_to_f16x2(r0, a[0], a[2]);
+            e4m3x4_to_f16x2(r1, a[1], a[3]);
+            e4m3x4_to_f16x2(r2, b[0], b[2]);
+            e4m3x4_to_f16x2(r3, b[1], b[3]);
 #pragma unroll
             for (int jj = 0; jj < kTilesPerHead; ++jj) {
               const int j = PK == 2 ? h : jj;
@@ -286,10 +291,11 @@ struct WarpState {
             // Low half: dim 2g of both tokens (row g); high half: dim 2g+1 (row g+8).
             const uint32_t e0 = __byte_perm(r0, 0u, 0x3120), e1 = __byte_perm(r1, 0u, 0x3120);
             const uint32_t e2 = __byte_perm(r2, 0u, 0x3120), e3 = __byte_perm(r3, 0u, 0x3120);
-            const uint32_t a[4] = {e4m3x2_to_f16x2(e0), e4m3x2_to_f16x2(e0 >> 16), e4m3x2_to_f16x2(e1),
-                                   e4m3x2_to_f16x2(e1 >> 16)};
-            const uint32_t b[4] = {e4m3x2_to_f16x2(e2), e4m3x2_to_f16x2(e2 >> 16), e4m3x2_to_f16x2(e3),
-                                   e4m3x2_to_f16x2(e3 >> 16)};
+            uint32_t a[4], b[4];
+            e4m3x4_to_f16x2(e0, a[0], a[1]);
+            e4m3x4_to_f16x2(e1, a[2], a[3]);
+            e4m3x4_to_f16x2(e2, b[0], b[1]);
+            e4m3x4_to_f16x2(e3, b[2], b[3]);
 #pragma unroll
             for (int jj = 0; jj < kTilesPerHead; ++jj) {
               const int j = PK == 2 ? h : jj;
