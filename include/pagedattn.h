@@ -322,6 +322,26 @@ PA_API int pa_chunk_prefill_fp8(const void* q, int64_t q_s0, int64_t q_s1, const
                                 int num_q_heads, float scale, int dtype, float k_scale, float v_scale, void* stream);
 
 /*
+ * ModelBatch metadata on the device: positions, KV slots, cumulative query
+ * starts, context lengths and padded block tables of one scheduler step.
+ *
+ * Replaces the tensor assembly of build_model_batch
+ * (runtime/model_runner.py:37-143; slots :56-66, padding :117-129).
+ * `packed` (device, int64) holds for R = num_requests requests: first
+ * scheduled position [R], scheduled tokens [R], block-table offset [R] and
+ * length [R], then the concatenated block tables (num_table_entries), then
+ * the total_tokens token ids in request order.  Outputs (device, int64):
+ * query_start_loc[R + 1], positions[T], context_lens[R] (= position +
+ * scheduled), block_tables[R][width] padded with -1, slot_mapping[T],
+ * input_token_ids[T].  A position past its request's table gets slot -1
+ * and PA_ERR_INVALID in *status (device int, may be null).
+ */
+PA_API int pa_build_batch_metadata(const int64_t* packed, int num_requests, int64_t num_table_entries,
+                                   int64_t total_tokens, int block_size, int64_t width, int64_t* query_start_loc,
+                                   int64_t* positions, int64_t* context_lens, int64_t* block_tables,
+                                   int64_t* slot_mapping, int64_t* input_token_ids, int* status, void* stream);
+
+/*
  * FP32 P.V accumulator: out[b, d] = sum_n p[b, n] * v[b, n, d] for N = 64,
  * D = 256, contiguous inputs.
  *

@@ -74,6 +74,11 @@ SIGNATURES: dict[str, tuple] = {
          _i32, _i32, _i32, _c_void_p, _i64, _i64, _i32, _i64, _i32, _i32, _f32, _i32, _c_void_p, _c_void_p],
     ),
     "pa_accumulate_pv": (_i32, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "pa_build_batch_metadata": (
+        _i32,
+        [_c_void_p, _i32, _i64, _i64, _i32, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+         _c_void_p, _c_void_p],
+    ),
     "pa_decode_noalloc_status": (_i32, [_c_void_p, _c_void_p]),
     "pa_kv_scatter_fp8": (
         _i32,

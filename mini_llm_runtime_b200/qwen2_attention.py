@@ -257,11 +257,21 @@ class Qwen2Attention(nn.Module):
         host = torch.cat([position_ids[:, 0], slot_mapping, context_lens, block_tables.reshape(-1)]).cpu().numpy()
         check_decode_metadata(host[2 * batch:3 * batch], host[3 * batch:].reshape(batch, w), host[batch:2 * batch],
                               host[:batch], kv_cache.block_size, kv_cache.num_blocks)
+        fused = new_token_blocks_private(host[2 * batch:3 * batch], host[3 * batch:].reshape(batch, w),
+                                         kv_cache.block_size)
+        return self.decode_batch_planned(hidden_states, position_ids, kv_cache, layer_idx, slot_mapping,
+                                         block_tables, context_lens, fused)
+
+    def decode_batch_planned(self, hidden_states, position_ids, kv_cache: PagedKVCache, layer_idx: int,
+                             slot_mapping, block_tables, context_lens, fused: bool) -> torch.Tensor:
+        """The compute of forward_decode_batch_with_cache on metadata the
+        caller has already checked (once per scheduler step, for every
+        layer): no device->host copy.  ``fused`` (new_token_blocks_private of
+        the step's metadata) selects the one-launch KV write + decode."""
+        batch = hidden_states.shape[0]
         k_layer, v_layer = kv_cache.get_layer_cache(layer_idx)
         q, k, v = self.project(hidden_states, position_ids)
-        lens_h = host[2 * batch:3 * batch]
-        if new_token_blocks_private(lens_h, host[3 * batch:].reshape(batch, w), kv_cache.block_size):
-            # KV write and decode in one launch (slots checked above).
+        if fused:
             out = paged_decode_with_kv_write(q.squeeze(1), k.squeeze(1), v.squeeze(1), slot_mapping, k_layer,
                                              v_layer, block_tables, context_lens, kv_cache.block_size,
                                              **_scales(kv_cache, layer_idx))
@@ -363,11 +373,20 @@ class Qwen2Attention(nn.Module):
             raise ValueError("slot_mapping must match block_tables and positions")
         if np.unique(slots).size != total:
             raise ValueError("slot_mapping must contain distinct slots")
+        return self.prefill_batch_planned(hidden_states, position_ids, kv_cache, layer_idx, slot_mapping,
+                                          query_start_loc, block_tables, context_lens,
+                                          int(chunks.max()) if nseq else 0)
+
+    def prefill_batch_planned(self, hidden_states, position_ids, kv_cache: PagedKVCache, layer_idx: int,
+                              slot_mapping, query_start_loc, block_tables, context_lens, max_q: int) -> torch.Tensor:
+        """The compute of forward_prefill_batch_with_cache on metadata the
+        caller has already checked: no device->host copy.  ``max_q`` is the
+        longest chunk."""
+        total = hidden_states.shape[1]
         k_layer, v_layer = kv_cache.get_layer_cache(layer_idx)
         q, k, v = self.project(hidden_states, position_ids)
         kv_cache.write_slots(slot_mapping=slot_mapping, k=k.squeeze(0), v=v.squeeze(0), layer_idx=layer_idx,
                              validate=False)
-        max_q = int(chunks.max()) if nseq else 0
         out = paged_attention_prefill_varlen(q.squeeze(0), query_start_loc, context_lens, block_tables, k_layer,
                                              v_layer, max_q, **_scales(kv_cache, layer_idx))
         return self.o_proj(out.reshape(1, total, self.hidden_size))

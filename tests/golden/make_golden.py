@@ -23,6 +23,11 @@ with the reference's outputs to ``tests/golden/*.npz``:
 * write_slots.npz     — tests/runtime/test_write_slots_batch.py cases for
   FP32/FP16/BF16 pools from a non-contiguous FP32 source (bit patterns).
 * accumulator.npz     — tests/kernels/test_accumulator_cuda.py expected value.
+* runner_steps.npz    — three scheduler steps (whole prompts; a prompt with
+  decodes; decodes) of the reference's TinyQwen2ForCausalLM through its
+  build_model_batch and execute_model_batch (runtime/model_runner.py:37-272)
+  on the seeded model and requests of tests/golden/runner_model.py: the
+  ModelBatch tensors, packed logits, greedy tokens and the written KV rows.
 
 The .npz files are committed; this script is how they were made.
 """
@@ -293,16 +298,65 @@ def gen_accumulator():
     np.savez_compressed(HERE / "accumulator.npz", p=p.numpy(), v=v.numpy(), out=expected.numpy())
 
 
+def gen_runner_steps(ref):
+    sys.path.insert(0, str(HERE))
+    import runner_model as M
+
+    config = ref["TinyQwen2Config"](**M.CONFIG)
+    model = ref["TinyQwen2ForCausalLM"](config)
+    model.load_state_dict(M.weights(), strict=True)
+    model.eval()
+    cache = ref["PagedKVCache"](M.CONFIG["num_hidden_layers"], M.NUM_BLOCKS, M.BLOCK_SIZE,
+                                M.CONFIG["num_key_value_heads"], M.CONFIG["hidden_size"] // M.CONFIG["num_attention_heads"],
+                                dtype=torch.float32, device="cpu")
+    prompts, tables = M.prompts(), M.block_tables()
+    reqs = {}
+    for rid in M.PROMPT_LENS:
+        reqs[rid] = ref["Request"](request_id=rid, prompt_token_ids=prompts[rid], max_new_tokens=8, arrival_time=0.0)
+        reqs[rid].block_table = list(tables[rid])
+    arrays = {}
+    for s, (pre, dec) in enumerate(M.STEPS):
+        sched = {rid: (len(prompts[rid]) - reqs[rid].num_computed_tokens) for rid in pre}
+        sched.update({rid: 1 for rid in dec})
+        out = ref["SchedulerOutput"](prefill_requests=[reqs[r] for r in pre], decode_requests=[reqs[r] for r in dec],
+                                     num_scheduled_tokens=sched)
+        batch = ref["build_model_batch"](out, M.BLOCK_SIZE, "cpu")
+        with torch.no_grad():
+            logits = ref["execute_model_batch"](model, batch, cache)
+        qsl = batch.query_start_loc.tolist()
+        sampled = [int(logits[qsl[i + 1] - 1].argmax()) for i in range(len(batch.request_ids))]
+        for name in ("input_token_ids", "positions", "query_start_loc", "context_lens", "block_tables",
+                     "slot_mapping"):
+            arrays[f"s{s}_{name}"] = getattr(batch, name).numpy()
+        arrays[f"s{s}_request_ids"] = np.array(batch.request_ids)
+        arrays[f"s{s}_logits"] = logits.numpy()
+        arrays[f"s{s}_sampled"] = np.array(sampled, dtype=np.int64)
+        for i, rid in enumerate(batch.request_ids):
+            reqs[rid].num_computed_tokens += sched[rid]
+            reqs[rid].output_token_ids.append(sampled[i])
+    # The pool rows the steps wrote: [L, slots, Hkv, D] at the sorted written slots.
+    written = np.unique(np.concatenate([arrays[f"s{s}_slot_mapping"] for s in range(len(M.STEPS))]))
+    arrays["written_slots"] = written
+    arrays["k_written"] = cache.k_cache.flatten(1, 2)[:, written].numpy()
+    arrays["v_written"] = cache.v_cache.flatten(1, 2)[:, written].numpy()
+    np.savez_compressed(HERE / "runner_steps.npz", **arrays)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref-src", default=os.environ.get("MINI_LLM_RUNTIME_SRC"),
                     help="src/ directory of a mini-llm-runtime checkout (or set MINI_LLM_RUNTIME_SRC)")
+    ap.add_argument("--only", default=None, help="generate only this fixture (file stem)")
     args = ap.parse_args()
     if not args.ref_src:
         ap.error("--ref-src (or MINI_LLM_RUNTIME_SRC) is required")
     sys.path.insert(0, args.ref_src)
     from mini_llm_runtime.kernels.reference import paged_attention as pa_ref
     from mini_llm_runtime.runtime.paged_kv_cache import PagedKVCache
+    from mini_llm_runtime.model.qwen2 import TinyQwen2Config, TinyQwen2ForCausalLM
+    from mini_llm_runtime.runtime.model_runner import build_model_batch, execute_model_batch
+    from mini_llm_runtime.runtime.request import Request
+    from mini_llm_runtime.runtime.scheduler import SchedulerOutput
 
     ref = {
         "PagedKVCache": PagedKVCache,
@@ -310,15 +364,27 @@ def main() -> None:
         "decode_reference": pa_ref.paged_attention_decode_batch_reference,
         "prefill_tiled": pa_ref.paged_attention_prefill_chunk_tiled,
         "prefill_tiled_reference": pa_ref.paged_attention_prefill_chunk_tiled_reference,
+        "TinyQwen2Config": TinyQwen2Config,
+        "TinyQwen2ForCausalLM": TinyQwen2ForCausalLM,
+        "build_model_batch": build_model_batch,
+        "execute_model_batch": execute_model_batch,
+        "Request": Request,
+        "SchedulerOutput": SchedulerOutput,
     }
     torch.set_num_threads(1)
-    gen_decode_config1(ref)
-    gen_decode_small(ref)
-    gen_decode_bf16(ref)
-    gen_prefill_small(ref)
-    gen_prefill_medium(ref)
-    gen_write_slots(ref)
-    gen_accumulator()
+    gens = {
+        "decode_config1": lambda: gen_decode_config1(ref),
+        "decode_small": lambda: gen_decode_small(ref),
+        "decode_bf16": lambda: gen_decode_bf16(ref),
+        "prefill_small": lambda: gen_prefill_small(ref),
+        "prefill_medium": lambda: gen_prefill_medium(ref),
+        "write_slots": lambda: gen_write_slots(ref),
+        "accumulator": gen_accumulator,
+        "runner_steps": lambda: gen_runner_steps(ref),
+    }
+    for name, gen in gens.items():
+        if args.only in (None, name):
+            gen()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 
