@@ -76,6 +76,43 @@ def parse_args():
     return ap.parse_args()
 
 
+def run_env() -> dict:
+    """What produced the numbers: source and library hashes (the GPU box has
+    no .git), the git HEAD when readable, and the toolchain and device."""
+    import hashlib
+    import platform
+
+    root = Path(__file__).resolve().parent
+    pkg = root / "mini_llm_runtime_b200"
+    h = hashlib.sha256()
+    for f in sorted([*pkg.glob("*.py"), *(pkg / "csrc").glob("*.cu*"), *(root / "include").glob("*.h")]):
+        h.update(f.name.encode())
+        h.update(f.read_bytes())
+    so = pkg / "libpagedattn.so"
+    env = {"source_sha256": h.hexdigest()[:16],
+           "library_sha256": hashlib.sha256(so.read_bytes()).hexdigest()[:16] if so.exists() else None,
+           "python": platform.python_version(), "torch": torch.__version__, "torch_cuda": torch.version.cuda,
+           "nccl": ".".join(map(str, torch.cuda.nccl.version())) if torch.cuda.is_available() else None}
+    head = root / ".git" / "HEAD"
+    if head.exists():
+        ref = head.read_text().strip()
+        if ref.startswith("ref: "):
+            ref_file = root / ".git" / ref[5:]
+            ref = ref_file.read_text().strip() if ref_file.exists() else ref
+        env["git_head"] = ref[:12]
+    if torch.cuda.is_available():
+        env["gpu"] = torch.cuda.get_device_name(0)
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            env["driver"] = pynvml.nvmlSystemGetDriverVersion()
+            pynvml.nvmlShutdown()
+        except Exception:  # noqa: BLE001 - the record is informational
+            pass
+    return env
+
+
 def env_rank():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -472,6 +509,7 @@ def run_reference(args, rank, world):
         "config": bench_config(world, r["batch"]),
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample", "spread")},
         "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "env": run_env(),
     }
     print(json.dumps(line), flush=True)
 
@@ -800,6 +838,7 @@ def main():
             "gpu_launches": args.steps * g_dev.launches_per_step,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "env": run_env(),
         }
         print(json.dumps(line), flush=True)
     # Graphs go before the process group.
