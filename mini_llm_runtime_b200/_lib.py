@@ -7,6 +7,7 @@ for any op in this package.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -150,8 +151,40 @@ def require_cuda(*tensors: torch.Tensor, what: str) -> torch.device:
     return dev
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The current stream of `device` as a raw cudaStream_t (an op's launch
+    stream), without building a torch.cuda.Stream object."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if _raw_stream is not None:
+        return _raw_stream(idx)
+    return torch.cuda.current_stream(idx).cuda_stream
+
+
+def device_guard(device: torch.device):
+    """torch.cuda.device(device), entered only when it is not already the
+    current device (the common case costs one query, not a switch and back)."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
+_ws_size_cache: dict[tuple, int] = {}
+
+
+def decode_workspace_bytes(batch: int, hkv: int, hq: int, d: int, bs: int, width: int, partition: int,
+                           code: int) -> int:
+    """pa_decode_workspace_bytes, memoised (a pure function of its arguments)."""
+    key = (batch, hkv, hq, d, bs, width, partition, code)
+    n = _ws_size_cache.get(key)
+    if n is None:
+        n = load().pa_decode_workspace_bytes(*key)
+        if len(_ws_size_cache) > 4096:
+            _ws_size_cache.clear()
+        _ws_size_cache[key] = n
+    return n
 
 
 def dtype_code(dtype: torch.dtype) -> int:
@@ -271,7 +304,8 @@ def prepare_workspace(ws: "_Workspace", batch: int, num_q_heads: int) -> None:
 
 
 def decode_workspace(device: torch.device, nbytes: int, batch: int, num_q_heads: int) -> torch.Tensor:
-    key = (device.index if device.index is not None else torch.cuda.current_device(), stream_handle(device))
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, stream_handle(device))
     ws = _workspaces.get(key)
     if ws is None or ws.tensor.numel() < nbytes:
         ws = _Workspace(device, nbytes)  # zeroed on the current stream

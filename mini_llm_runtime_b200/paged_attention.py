@@ -54,6 +54,8 @@ def _pool_ok(k_cache: torch.Tensor, v_cache: torch.Tensor, dtype: torch.dtype) -
 
 
 def _as_long(t: torch.Tensor, device: torch.device) -> torch.Tensor:
+    if isinstance(t, torch.Tensor) and t.dtype is torch.long and t.device == device:
+        return t
     t = torch.as_tensor(t, device=device)
     if t.dtype != torch.long:
         t = t.long()
@@ -83,13 +85,13 @@ def _decode_launch(
     seq_lens = seq_lens.contiguous()
     code = _lib.dtype_code(q.dtype)
     width = block_tables.shape[1]
-    ws_bytes = lib.pa_decode_workspace_bytes(b, hkv, hq, d, bs, width, partition_tokens, code)
+    ws_bytes = _lib.decode_workspace_bytes(b, hkv, hq, d, bs, width, partition_tokens, code)
     if ws_bytes == 0:
         raise ValueError("invalid decode arguments")
     ws = _lib.decode_workspace(dev, ws_bytes, b, hq)
     if scale is None:
         scale = 1.0 / math.sqrt(d)
-    with torch.cuda.device(dev):
+    with _lib.device_guard(dev):
         if k_cache.dtype == _lib.FP8_DTYPE:
             st = lib.pa_paged_decode_fp8(
                 q.data_ptr(), q.stride(0), q.stride(1), None, None, None,
@@ -168,13 +170,13 @@ def paged_decode_with_kv_write(
     out = torch.empty((b, hq, d), dtype=q.dtype, device=dev)
     code = _lib.dtype_code(q.dtype)
     width = block_tables.shape[1]
-    ws_bytes = lib.pa_decode_workspace_bytes(b, hkv, hq, d, bs, width, 0, code)
+    ws_bytes = _lib.decode_workspace_bytes(b, hkv, hq, d, bs, width, 0, code)
     if ws_bytes == 0:
         raise ValueError("invalid decode arguments")
     ws = _lib.decode_workspace(dev, ws_bytes, b, hq)
     if scale is None:
         scale = 1.0 / math.sqrt(d)
-    with torch.cuda.device(dev):
+    with _lib.device_guard(dev):
         if fp8:
             st = lib.pa_paged_decode_fp8(
                 q.data_ptr(), q.stride(0), q.stride(1), new_k.data_ptr(), new_v.data_ptr(), slots.data_ptr(),
@@ -356,7 +358,7 @@ def _prefill_launch(
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     cu_q_lens, context_lens = cu_q_lens.contiguous(), context_lens.contiguous()
-    with torch.cuda.device(dev):
+    with _lib.device_guard(dev):
         if k_cache.dtype == _lib.FP8_DTYPE:
             st = lib.pa_chunk_prefill_fp8(
                 q.data_ptr(), q.stride(0), q.stride(1), cu_q_lens.data_ptr(), context_lens.data_ptr(),
@@ -481,7 +483,7 @@ def paged_attention_accumulator_cuda(p: torch.Tensor, v: torch.Tensor) -> torch.
     p = p.contiguous()
     v = v.contiguous()
     out = torch.empty((p.shape[0], 256), dtype=torch.float32, device=p.device)
-    with torch.cuda.device(dev):
+    with _lib.device_guard(dev):
         st = _lib.load().pa_accumulate_pv(p.data_ptr(), v.data_ptr(), out.data_ptr(), p.shape[0],
                                           _lib.stream_handle(dev))
     _lib.check(st, "pa_accumulate_pv")

@@ -219,7 +219,7 @@ class PagedKVCache:
             layer_k, layer_v = self.k_cache[layer_idx], self.v_cache[layer_idx]
             slot_mapping = slot_mapping.contiguous()
             ks, vs = self.layer_scales(layer_idx)
-            with torch.cuda.device(dev):
+            with _lib.device_guard(dev):
                 st = lib.pa_kv_scatter_fp8(
                     k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
                     v.data_ptr(), v.stride(0), v.stride(1), v.stride(2), _lib.dtype_code(k.dtype),
@@ -236,7 +236,7 @@ class PagedKVCache:
         layer_v = self.v_cache[layer_idx]
         if not slot_mapping.is_contiguous():
             slot_mapping = slot_mapping.contiguous()
-        with torch.cuda.device(dev):
+        with _lib.device_guard(dev):
             st = lib.pa_kv_scatter(
                 k.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
                 v.data_ptr(), v.stride(0), v.stride(1), v.stride(2), _lib.dtype_code(k.dtype),
