@@ -71,8 +71,9 @@ def parse_args():
                     help="time one kernel case alone (secondary configs; the small ncu targets)")
     ap.add_argument("--layers", type=int, default=None, help="layers the --kernel case rotates over")
     ap.add_argument("--reps", type=int, default=None, help="graph replays timed by the --kernel case")
-    ap.add_argument("--mode", choices=["request-shard", "head-shard"], default="request-shard",
-                    help="head-shard: config 3 split by KV head over the GPUs, NCCL all-gather of head outputs")
+    ap.add_argument("--mode", choices=["request-shard", "head-shard", "mixed"], default="request-shard",
+                    help="head-shard: config 3 split by KV head over the GPUs, NCCL all-gather of head outputs; "
+                         "mixed: config 5 as one prefill + decode step per layer, sharded by request")
     return ap.parse_args()
 
 
@@ -678,6 +679,132 @@ def run_head_shard(args, rank, world, local_rank):
     dist.destroy_process_group()
 
 
+def run_mixed(args, rank, world, local_rank):
+    """BASELINE config 5 as one mixed step: per layer, the prefill chunks'
+    KV write (pa_kv_scatter), one batched chunk-prefill (pa_chunk_prefill,
+    tcgen05) and one decode with the fused KV write (balanced kernel), 28
+    layers at 28/4 heads, D 128, bs 16; random Q/K/V ~ N(0, 1).  Requests are
+    sharded over the ranks longest first (decodes by context, chunks by
+    causal work).  One CUDA graph per step; the same layers as decode-only
+    and prefill-only graphs give the split.  `value` is the whole job's
+    decode KV GB/s; time is the max over ranks."""
+    from mini_llm_runtime_b200 import PagedKVCache, _lib, paged_attention_prefill_varlen, paged_decode_with_kv_write
+    from mini_llm_runtime_b200.sharding import decode_cost, prefill_cost, shard_requests
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29541")
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=device)
+    _lib.load()
+    L5, HQ5, HKV5, D5 = 28, 28, 4, 128
+    ctx_all = np.random.default_rng(5).integers(256, 8193, size=256).astype(np.int64)
+    prefix_all = np.random.default_rng(6).integers(0, 4097, size=4).astype(np.int64)
+    chunk_all = np.full(4, 1024, dtype=np.int64)
+    dec = shard_requests([decode_cost(c) for c in ctx_all], world)[rank].requests
+    pre = shard_requests([prefill_cost(p, c) for p, c in zip(prefix_all, chunk_all)], world)[rank].requests
+    ctx_d = ctx_all[dec]
+    prefix, chunk = prefix_all[pre], chunk_all[pre]
+    ctx_p = prefix + chunk
+    nd, npf = len(ctx_d), len(pre)
+    rng = np.random.default_rng(500 + rank)
+    tables, nb = _random_tables(rng, np.concatenate([ctx_d, ctx_p]), BS)
+    cache = PagedKVCache(L5, nb, BS, HKV5, D5, dtype=torch.bfloat16, device=device)
+    gen = torch.Generator(device=device).manual_seed(600 + rank)
+    cache.k_cache.normal_(generator=gen)
+    cache.v_cache.normal_(generator=gen)
+    bt = torch.tensor(tables, device=device)
+    bt_d, bt_p = bt[:nd], bt[nd:]
+    cl_d = torch.tensor(ctx_d, device=device)
+    cl_p = torch.tensor(ctx_p, device=device)
+    pos_d = ctx_d - 1
+    slots_d = torch.tensor(tables[np.arange(nd), pos_d // BS] * BS + pos_d % BS, device=device)
+    tp = int(chunk.sum())
+    seq_p = np.repeat(np.arange(npf), chunk)
+    pos_p = (np.arange(tp) - np.concatenate([[0], np.cumsum(chunk)[:-1]])[seq_p] + prefix[seq_p]) if tp else seq_p
+    slots_p = torch.tensor(tables[nd + seq_p, pos_p // BS] * BS + pos_p % BS, device=device) if tp else None
+    cu_p = torch.tensor(np.concatenate([[0], np.cumsum(chunk)]), device=device)
+    q_d = _bf16_randn((L5, nd, HQ5, D5), device, gen)
+    nk_d = _bf16_randn((L5, nd, HKV5, D5), device, gen)
+    nv_d = _bf16_randn((L5, nd, HKV5, D5), device, gen)
+    q_p = _bf16_randn((L5, tp, HQ5, D5), device, gen) if tp else None
+    k_p = _bf16_randn((L5, tp, HKV5, D5), device, gen) if tp else None
+    v_p = _bf16_randn((L5, tp, HKV5, D5), device, gen) if tp else None
+    max_q = int(chunk.max()) if npf else 0
+
+    def body(do_prefill: bool, do_decode: bool):
+        for l in range(L5):
+            if do_prefill and tp:
+                cache.write_slots(slots_p, k_p[l], v_p[l], layer_idx=l, validate=False)
+                paged_attention_prefill_varlen(q_p[l], cu_p, cl_p, bt_p, cache.k_cache[l], cache.v_cache[l], max_q)
+            if do_decode and nd:
+                paged_decode_with_kv_write(q_d[l], nk_d[l], nv_d[l], slots_d, cache.k_cache[l], cache.v_cache[l],
+                                           bt_d, cl_d, BS)
+
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        body(True, True)
+    torch.cuda.synchronize()
+
+    def time_graph(do_prefill: bool, do_decode: bool) -> float:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            body(do_prefill, do_decode)
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del graph
+        t = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64, device=device)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = {"step": time_graph(True, True), "decode_only": time_graph(False, True),
+          "prefill_only": time_graph(True, False)}
+    _lib.check_device_status(device)
+    kv_total = int(ctx_all.sum()) * HKV5 * D5 * 2 * 2 * L5  # decode KV bytes per step, all ranks
+    flops_total = prefill_flops(prefix_all, chunk_all, HQ5, D5) * L5
+    kv_rank = int(ctx_d.sum()) * HKV5 * D5 * 2 * 2 * L5
+    flops_rank = prefill_flops(prefix, chunk, HQ5, D5) * L5 if npf else 0
+    ideal = torch.tensor([(kv_rank / (hbm_peak()[0] * 1e9) + flops_rank / (bf16_peak()[0] * 1e12)) * 1e3],
+                         dtype=torch.float64, device=device)
+    if dist is not None:
+        dist.all_reduce(ideal, op=dist.ReduceOp.MAX)
+    if rank == 0:
+        step_s = ms["step"] * 1e-3
+        print(json.dumps({
+            "mode": "mixed", "metric": METRIC, "value": kv_total / step_s / 1e9, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms["step"], "higher_is_better": True,
+            "scaling": "strong", "dtype": "bf16", "data": "synthetic",
+            "prefill_tflops": flops_total / step_s / 1e12,
+            "tok_per_s": (len(ctx_all) + int(chunk_all.sum())) / step_s,
+            "ms_decode_only": ms["decode_only"], "ms_prefill_only": ms["prefill_only"],
+            "roofline": {"ideal_ms": float(ideal.item()), "frac": float(ideal.item()) / ms["step"],
+                         "model": "max over ranks of (decode KV bytes / measured HBM peak + prefill FLOPs / "
+                                  "measured BF16 peak), the two in sequence"},
+            "config": {"workload": "config5: mixed step, 28 layers x (prefill KV write + chunk-prefill of 4 x 1024 "
+                                   "on prefix U[0,4096] + decode with fused KV write of 256 seqs, ctx U[256,8192]), "
+                                   "28/4 heads, D128, bs16, requests sharded longest first",
+                       "parallelism": f"request-sharded dp{world}, no communication"}}), flush=True)
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
     rank, world, local_rank = env_rank()
@@ -689,6 +816,9 @@ def main():
         return
     if args.mode == "head-shard":
         run_head_shard(args, rank, world, local_rank)
+        return
+    if args.mode == "mixed":
+        run_mixed(args, rank, world, local_rank)
         return
 
     import torch.distributed as dist
