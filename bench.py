@@ -931,13 +931,22 @@ def main():
                 traffic = float(line.split(":", 1)[1])
 
     # ---- secondary configs, one kernel at a time (same GPU, after the step) --
+    # With N > 1 every rank times the same case on its own GPU at the same
+    # time, and the slowest rank's launch time is reported.
     secondary = {}
-    if world == 1:
-        for name in ("split-config3", "prefill-config4", "decode-config5", "prefill-config5", "decode-config2-fp8",
-                     "decode-config5-fp8"):
-            r = time_kernel_case(name, device)
-            secondary[name] = {k: r[k] for k in ("workload", "us_per_launch", "achieved", "unit", "frac")}
-            torch.cuda.empty_cache()
+    for name in ("split-config3", "prefill-config4", "decode-config5", "prefill-config5", "decode-config2-fp8",
+                 "decode-config5-fp8"):
+        barrier()
+        r = time_kernel_case(name, device)
+        entry = {k: r[k] for k in ("workload", "us_per_launch", "achieved", "unit", "frac")}
+        if world > 1:
+            us = reduce(r["us_per_launch"], dist.ReduceOp.MAX)
+            scale = 1e9 if r["bound"] == "hbm" else 1e12
+            entry.update(us_per_launch=us, achieved=r["work_per_launch"] / (us * 1e-6) / scale,
+                         ranks=world, timing="max over ranks, every rank running the case at once")
+            entry["frac"] = entry["achieved"] / r["peak"]
+        secondary[name] = entry
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
