@@ -72,7 +72,8 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None, help="layers the --kernel case rotates over")
     ap.add_argument("--reps", type=int, default=None, help="graph replays timed by the --kernel case")
     ap.add_argument("--mode", choices=["request-shard", "head-shard", "mixed"], default="request-shard",
-                    help="head-shard: config 3 split by KV head over the GPUs, NCCL all-gather of head outputs; "
+                    help="head-shard: config 3 split by KV head over the GPUs, all-gather of head outputs over "
+                         "NVLink peer stores (and, for comparison, NCCL); "
                          "mixed: config 5 as one prefill + decode step per layer, sharded by request")
     return ap.parse_args()
 
@@ -601,9 +602,12 @@ def run_per_layer_e2e(w: dict, device, steps: int, warmup: int, barrier) -> dict
 def run_head_shard(args, rank, world, local_rank):
     """Config 3 (8 x 32,768 tokens, 14/2 heads) decoded with its KV heads split
     over the ranks: each rank streams its heads' KV from its own pools and one
-    NCCL all-gather per layer rebuilds [B, Hq, D].  Layers x (decode +
-    all-gather) are captured in one CUDA graph; `value` is the whole batch's
-    algorithmic KV bytes per second (max over ranks)."""
+    all-gather per layer rebuilds [B, Hq, D].  The all-gather runs two ways:
+    pa_head_allgather (peer stores over NVLink and a flag handshake, the
+    default `transport="peer"`) and NCCL's all_gather_into_tensor.  Layers x
+    (decode + all-gather) are captured in one CUDA graph; `value` is the whole
+    batch's algorithmic KV bytes per second with the peer all-gather (max over
+    ranks)."""
     import torch.distributed as dist
 
     from mini_llm_runtime_b200 import _lib
@@ -626,54 +630,68 @@ def run_head_shard(args, rank, world, local_rank):
     v = _bf16_randn((layers, nb, BS, hkv_l, D), device, gen)
     q = _bf16_randn((layers, len(ctx), hq_l, D), device, gen)
     bt, cl = torch.tensor(tables, device=device), torch.tensor(ctx, device=device)
-    hs = HeadShardedDecode(HQ, HKV)
     out = torch.empty(layers, len(ctx), HQ, D, dtype=torch.bfloat16, device=device)
     part = torch.empty(layers, world, len(ctx), hq_l, D, dtype=torch.bfloat16, device=device)
-
-    def body(gather_only=False):
-        for l in range(layers):
-            if gather_only:
-                dist.all_gather_into_tensor(part[l], q[l].contiguous())
-            else:
-                hs(q[l], k[l], v[l], bt, cl, BS, out=out[l])
-
     s = torch.cuda.Stream(device)
     s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        body()
-        body(True)
-    torch.cuda.synchronize()
-    def time_graph(gather_only: bool) -> float:
-        # The graph holds NCCL calls: it must be gone before the process
-        # group is destroyed, so it lives only inside this function.
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=s):
-            body(gather_only)
-        for _ in range(max(args.warmup, 3)):
-            graph.replay()
-        dist.barrier(device_ids=[local_rank])
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        del graph
-        t = torch.tensor([e0.elapsed_time(e1) / (args.steps * layers)], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
-    times = {"step": time_graph(False), "gather": time_graph(True)}
+    def measure(transport: str) -> dict:
+        hs = HeadShardedDecode(HQ, HKV, transport=transport, max_batch=len(ctx))
+
+        def body(gather_only=False):
+            for l in range(layers):
+                if not gather_only:
+                    hs(q[l], k[l], v[l], bt, cl, BS, out=out[l])
+                elif transport == "peer":
+                    hs._peer(q[l], out[l])
+                else:
+                    dist.all_gather_into_tensor(part[l], q[l].contiguous())
+
+        with torch.cuda.stream(s):
+            body()  # the peer transport maps the peers' exchange areas here
+            body(True)
+        torch.cuda.synchronize()
+
+        def time_graph(gather_only: bool) -> float:
+            # A graph holding NCCL calls must be gone before the process group
+            # is destroyed, so it lives only inside this function.
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=s):
+                body(gather_only)
+            for _ in range(max(args.warmup, 3)):
+                graph.replay()
+            dist.barrier(device_ids=[local_rank])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del graph
+            t = torch.tensor([e0.elapsed_time(e1) / (args.steps * layers)], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        r = {"step": time_graph(False), "gather": time_graph(True)}
+        hs.check()
+        hs.close()
+        return r
+
+    peer = measure("peer")
+    coll = measure("collective")
     torch.cuda.synchronize()
     kv = int(ctx.sum()) * HKV * D * 2 * 2
     if rank == 0:
         print(json.dumps({
-            "mode": "head-shard", "metric": METRIC, "value": kv / (times["step"] * 1e-3) / 1e9, "unit": UNIT,
+            "mode": "head-shard", "metric": METRIC, "value": kv / (peer["step"] * 1e-3) / 1e9, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
-            "data": "synthetic", "ms_per_layer": times["step"], "allgather_ms_per_layer": times["gather"],
+            "data": "synthetic", "ms_per_layer": peer["step"], "allgather_ms_per_layer": peer["gather"],
+            "transport": "pa_head_allgather: peer stores over NVLink + flag handshake, one kernel per layer",
+            "nccl": {"value": kv / (coll["step"] * 1e-3) / 1e9, "ms_per_layer": coll["step"],
+                     "allgather_ms_per_layer": coll["gather"]},
             "config": {"workload": "config3: 8 x 32768 tokens, 14/2 heads, D64, bs16, KV heads split over the "
-                                   "GPUs, NCCL all-gather of the [B, Hq/N, D] head outputs per layer",
+                                   "GPUs, all-gather of the [B, Hq/N, D] head outputs per layer",
                        "layers_in_graph": layers}}), flush=True)
     dist.barrier(device_ids=[local_rank])
     dist.destroy_process_group()

@@ -47,6 +47,7 @@ extern "C" {
  * bounded wait inside a kernel gives up (never expected in normal runs). */
 #define PA_DEVICE_TIMEOUT_TMA 101
 #define PA_DEVICE_TIMEOUT_MMA 102
+#define PA_DEVICE_TIMEOUT_PEER 103 /* a peer GPU did not raise its flag in time (pa_head_allgather) */
 
 /* Element types (torch dtype mapping in mini_llm_runtime_b200/_lib.py). */
 #define PA_DTYPE_F32 0
@@ -57,6 +58,10 @@ extern "C" {
 
 /* Flags of pa_paged_decode_ex. */
 #define PA_DECODE_EARLY_INPUTS 1 /* metadata and pools may be read before the PDL wait */
+
+/* Ranks and IPC handle size of the peer head all-gather. */
+#define PA_PEER_MAX_RANKS 8
+#define PA_IPC_HANDLE_BYTES 64
 
 /* Ints in the control block of pa_chunk_prefill. */
 #define PA_PREFILL_CONTROL_INTS 4
@@ -349,6 +354,46 @@ PA_API int pa_build_batch_metadata(const int64_t* packed, int num_requests, int6
  * (kernels/cuda/accumulator.py:21-37 -> paged_attention_accumulator.cu:72-90).
  */
 PA_API int pa_accumulate_pv(const float* p, const float* v, float* out, int64_t batch, void* stream);
+
+/*
+ * All-gather of attention head outputs over NVLink peer memory, for decode
+ * sharded by KV head across the GPUs of one node (rank r of `world` decodes
+ * query heads [r*heads_local, (r+1)*heads_local) of every sequence).
+ *
+ * Replaces, on the KV-head-sharded path, the all-gather of the [B, Hq/g, D]
+ * head outputs that torch.distributed / NCCL would run; the reference runs
+ * one process on one device (runtime/model_runner.py:146-288) and has no
+ * counterpart.  The per-rank decode it follows is
+ * paged_attention_decode_batch_parallel (kernels/reference/paged_attention.py:178-254).
+ *
+ * Each rank allocates one exchange area of pa_peer_gather_bytes(world,
+ * B_max * heads_local * head_dim * esize) bytes (256-byte aligned), zeroes it,
+ * exports it with pa_ipc_export, and maps every peer's area with
+ * pa_ipc_import; `areas` (HOST array of `world` device pointers) holds every
+ * rank's area as seen from this process, its own at [rank].  All ranks must
+ * have zeroed and mapped all areas before the first call (a host barrier).
+ *
+ * pa_head_allgather: part [batch, heads_local, head_dim] with element strides
+ * (p_s0, p_s1); out [batch, world*heads_local, head_dim] with (o_s0, o_s1);
+ * dtype F16/BF16/F32 (head_dim * esize, strides and pointers 16-byte
+ * aligned).  One kernel stores `part` into `out` and into every peer's area,
+ * raises this rank's flag in every peer's area (system-scope release), waits
+ * until every peer's flag reaches this call's number (bounded: wait_limit_ns,
+ * 0 = 500 ms; on expiry the area's status word at byte 136 becomes
+ * PA_DEVICE_TIMEOUT_PEER and `out` keeps only this rank's heads), then copies
+ * the peers' heads into `out`.  Every rank must make the same sequence of
+ * calls; calls on one rank must be ordered on one stream.  CUDA-graph capture
+ * works: the call number lives in the area, not in the launch arguments.
+ * After a timeout the exchange is out of step: zero the areas on every rank
+ * (between a host barrier and the next call) before reusing them.
+ */
+PA_API size_t pa_peer_gather_bytes(int world, int64_t slice_bytes);
+PA_API int pa_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+PA_API int pa_ipc_import(const void* handle, uint64_t offset, void** dev_ptr_out, void** base_out);
+PA_API int pa_ipc_close(void* base);
+PA_API int pa_head_allgather(const void* part, int64_t p_s0, int64_t p_s1, int batch, int heads_local, int head_dim,
+                             int dtype, int rank, int world, void* const* areas, int64_t area_bytes, void* out,
+                             int64_t o_s0, int64_t o_s1, int64_t wait_limit_ns, void* stream);
 
 #ifdef __cplusplus
 }

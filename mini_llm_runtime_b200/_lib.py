@@ -26,6 +26,9 @@ PA_ERR_CAPACITY = -5
 PA_DECODE_EARLY_INPUTS = 1
 PA_DEVICE_TIMEOUT_TMA = 101
 PA_DEVICE_TIMEOUT_MMA = 102
+PA_DEVICE_TIMEOUT_PEER = 103
+PA_PEER_MAX_RANKS = 8
+PA_IPC_HANDLE_BYTES = 64
 
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3, torch.float8_e4m3fn: 4}
 PA_DTYPE_FP8_E4M3 = 4
@@ -98,6 +101,15 @@ SIGNATURES: dict[str, tuple] = {
          _i32, _i32, _i32, _c_void_p, _i64, _i64, _i32, _i64, _i32, _i32, _f32, _i32, _f32, _f32, _c_void_p],
     ),
     "pa_selftest_wait_timeout": (_i32, [_c_void_p, _i64, _c_void_p]),
+    "pa_peer_gather_bytes": (_size, [_i32, _i64]),
+    "pa_ipc_export": (_i32, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
+    "pa_ipc_import": (_i32, [_c_void_p, ctypes.c_uint64, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p)]),
+    "pa_ipc_close": (_i32, [_c_void_p]),
+    "pa_head_allgather": (
+        _i32,
+        [_c_void_p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_c_void_p), _i64, _c_void_p,
+         _i64, _i64, _i64, _c_void_p],
+    ),
 }
 
 _lib = None

@@ -42,6 +42,12 @@
 
 #include "attn_generic.cuh"
 
+// Early-inputs launches warm L2 with the first piece's query rows before the
+// wait for the previous kernel (1) or not (0).
+#ifndef PA_DECODE_Q_PREFETCH
+#define PA_DECODE_Q_PREFETCH 1
+#endif
+
 namespace pa {
 namespace {
 
@@ -672,6 +678,20 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
   };
   int issued = 0;
   for (; issued < STAGES && issued < nj; ++issued) issue(issued);
+#if PA_DECODE_Q_PREFETCH
+  if (p.early && nj > 0) {
+    // The first piece's query rows go to L2 while the previous kernel
+    // finishes, so their load after the wait hits L2 instead of queueing in
+    // HBM behind every CTA's first ring copies.
+    const Seg s0 = seg_at(pre, p.B, p.SPS, lo);
+    int kvh0, h0, hn;
+    seg_heads<PK>(p, s0.segx, kvh0, h0, hn);
+    constexpr int kLines = (D * (int)sizeof(TQ) + 127) / 128;
+    const TQ* qrow = reinterpret_cast<const TQ*>(p.q) + (int64_t)s0.b * p.q_s0;
+    for (int i = lane; i < hn * kLines; i += 32)
+      prefetch_l2(qrow + (int64_t)(h0 + i / kLines) * p.q_s1 + (i % kLines) * (128 / (int)sizeof(TQ)));
+  }
+#endif
   if (p.early) grid_dep_wait();
 
   const TQ* qbase = reinterpret_cast<const TQ*>(p.q);

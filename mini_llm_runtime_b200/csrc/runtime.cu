@@ -80,8 +80,9 @@ extern "C" const char* pa_status_string(int status) {
     case PA_ERR_CAPACITY: return "request exceeds built-in capacity";
     case PA_DEVICE_TIMEOUT_TMA: return "device: bounded wait for a TMA copy gave up";
     case PA_DEVICE_TIMEOUT_MMA: return "device: bounded wait for a tensor-core step gave up";
+    case PA_DEVICE_TIMEOUT_PEER: return "device: bounded wait for a peer GPU's flag gave up";
     default: return "unknown status";
   }
 }
 
-extern "C" int pa_abi_version(void) { return 2; }
+extern "C" int pa_abi_version(void) { return 3; }

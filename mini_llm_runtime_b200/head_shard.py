@@ -12,9 +12,13 @@ every rank.  Each rank streams 1/g of the KV bytes; the all-gather moves
 ``B * Hq * D`` elements (14 KB for 8 sequences of Qwen2.5-0.5B geometry), so
 the collective is latency-bound, not bandwidth-bound.
 
-This is the one place a collective sits on the path: NCCL over NVLink
-(``torch.distributed``, backend "nccl"); the head outputs arrive through NCCL
-into local memory.  The reference runs one process on one device
+This is the one place an exchange between GPUs sits on the path.  By default
+(``transport="peer"`` on CUDA ranks) it is ``pa_head_allgather``: one kernel
+stores each rank's slice straight into every peer's memory over NVLink (CUDA
+IPC mappings set up once), raises a flag there, and waits (bounded) for the
+peers' flags: one launch and one NVLink round trip per layer.
+``transport="collective"`` runs ``torch.distributed`` all-gather instead (NCCL
+on GPUs, gloo on CPU ranks).  The reference runs one process on one device
 (runtime/model_runner.py:146-288), so it has no counterpart; the per-rank math
 is its paged_attention_decode_batch_parallel
 (kernels/reference/paged_attention.py:178-254) on a head slice.
@@ -22,10 +26,13 @@ is its paged_attention_decode_batch_parallel
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 
 def head_slices(num_q_heads: int, num_kv_heads: int, world_size: int, rank: int) -> tuple[slice, slice]:
@@ -46,6 +53,99 @@ def shard_pool(pool: torch.Tensor, kv_slice: slice) -> torch.Tensor:
     return pool[..., kv_slice, :].contiguous()
 
 
+class PeerHeadGather:
+    """All-gather of ``[B, heads_local, D]`` head outputs over NVLink peer
+    memory: ``pa_head_allgather`` on this rank's exchange area and its IPC
+    mappings of every peer's.  Construction is collective (every rank of
+    ``group`` builds one with the same arguments): it exports this rank's
+    area, maps every peer's and ends with a barrier.  Calls must follow the
+    same sequence on every rank; they may be captured in a CUDA graph."""
+
+    def __init__(self, group: dist.ProcessGroup | None, max_batch: int, heads_local: int, head_dim: int,
+                 dtype: torch.dtype, device: torch.device, wait_limit_ns: int = 0):
+        lib = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > _lib.PA_PEER_MAX_RANKS:
+            raise ValueError(f"at most {_lib.PA_PEER_MAX_RANKS} ranks share a peer all-gather")
+        self.device = torch.device(device)
+        self.max_batch, self.heads_local, self.head_dim, self.dtype = max_batch, heads_local, head_dim, dtype
+        self.wait_limit_ns = wait_limit_ns
+        esize = torch.empty((), dtype=dtype).element_size()
+        nbytes = lib.pa_peer_gather_bytes(self.world, max_batch * heads_local * head_dim * esize)
+        if nbytes == 0:
+            raise ValueError("invalid peer all-gather size")
+        # Above the caching allocator's 10 MB split limit the area gets a
+        # segment (one cudaMalloc) of its own: its IPC handle is distinct from
+        # every other area's, and a peer maps it exactly once.
+        self.area = torch.zeros(max(nbytes, 12 << 20), dtype=torch.uint8, device=self.device)
+        if self.area.data_ptr() % 256:
+            raise _lib.PagedAttentionError("exchange area is not 256-byte aligned")
+        handle = ctypes.create_string_buffer(_lib.PA_IPC_HANDLE_BYTES)
+        offset = ctypes.c_uint64()
+        _lib.check(lib.pa_ipc_export(self.area.data_ptr(), handle, ctypes.byref(offset)), "pa_ipc_export")
+        torch.cuda.synchronize(self.device)  # zeroed before any peer can write into it
+        infos: list = [None] * self.world
+        dist.all_gather_object(infos, (handle.raw, offset.value), group=group)
+        ptrs, self._bases = [], []
+        for r, (h, off) in enumerate(infos):
+            if r == self.rank:
+                ptrs.append(self.area.data_ptr())
+                continue
+            ptr, base = ctypes.c_void_p(), ctypes.c_void_p()
+            _lib.check(lib.pa_ipc_import(h, off, ctypes.byref(ptr), ctypes.byref(base)), "pa_ipc_import")
+            ptrs.append(ptr.value)
+            self._bases.append(base.value)
+        self._areas = (ctypes.c_void_p * self.world)(*ptrs)
+        self._nbytes = nbytes
+        self._barrier()  # every area is zeroed and mapped on every rank
+
+    def _barrier(self) -> None:
+        if dist.get_backend(self.group) == "nccl":
+            dist.barrier(group=self.group, device_ids=[self.device.index])
+        else:
+            dist.barrier(group=self.group)
+
+    def __call__(self, part: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """part [B, heads_local, D] -> out [B, world * heads_local, D]."""
+        b, hl, d = part.shape
+        if hl != self.heads_local or d != self.head_dim or b > self.max_batch or part.dtype != self.dtype:
+            raise ValueError("part does not match the exchange this all-gather was built for")
+        if tuple(out.shape) != (b, hl * self.world, d) or out.dtype != part.dtype:
+            raise ValueError("out must be [B, world * heads_local, D] of part's dtype")
+        if part.stride(2) != 1 or out.stride(2) != 1:
+            raise ValueError("head_dim must be contiguous")
+        _lib.check(
+            _lib.load().pa_head_allgather(
+                part.data_ptr(), part.stride(0), part.stride(1), b, hl, d, _lib.dtype_code(part.dtype), self.rank,
+                self.world, self._areas, self._nbytes, out.data_ptr(), out.stride(0), out.stride(1),
+                self.wait_limit_ns, _lib.stream_handle(part.device)),
+            "pa_head_allgather")
+        return out
+
+    def status(self) -> int:
+        """0, or PA_DEVICE_TIMEOUT_PEER when a wait for a peer gave up
+        (synchronises the device)."""
+        return int(self.area[136:140].view(torch.int32).item())
+
+    def check(self) -> None:
+        code = self.status()
+        if code:
+            raise _lib.PagedAttentionError(
+                f"peer all-gather: {_lib.load().pa_status_string(code).decode()} (status {code})")
+
+    def close(self) -> None:
+        """Unmap the peers' areas (collective: ends with a barrier, after which
+        each rank may free its own area)."""
+        torch.cuda.synchronize(self.device)
+        lib = _lib.load()
+        for base in self._bases:
+            _lib.check(lib.pa_ipc_close(base), "pa_ipc_close")
+        self._bases = []
+        self._barrier()
+
+
 class HeadShardedDecode:
     """Batched paged decode of this rank's KV heads plus the all-gather of the
     head outputs.
@@ -64,6 +164,8 @@ class HeadShardedDecode:
         num_kv_heads: int,
         group: dist.ProcessGroup | None = None,
         local_decode: Callable | None = None,
+        transport: str = "peer",
+        max_batch: int = 256,
     ):
         self.group = group
         self.world = dist.get_world_size(group)
@@ -74,6 +176,12 @@ class HeadShardedDecode:
             from .paged_attention import paged_attention_decode_batch_parallel as local_decode
         self.local_decode = local_decode
         self._nccl = dist.get_backend(group) == "nccl"
+        if transport not in ("peer", "collective"):
+            raise ValueError("transport must be 'peer' or 'collective'")
+        # The peer exchange needs CUDA ranks; CPU (gloo) ranks use the collective.
+        self.transport = transport if self._nccl else "collective"
+        self.max_batch = max_batch
+        self._peer: PeerHeadGather | None = None
 
     def local_queries(self, q: torch.Tensor) -> torch.Tensor:
         """This rank's query heads of a full ``[B, Hq, D]`` query."""
@@ -94,6 +202,17 @@ class HeadShardedDecode:
         if hq_local * self.world != self.hq or k_pool_local.shape[2] * self.world != self.hkv:
             raise ValueError("q_local / pools do not hold this rank's share of the heads")
         part = self.local_decode(q_local, k_pool_local, v_pool_local, block_tables, context_lens, block_size)
+        if self.transport == "peer":
+            if self._peer is None or self._peer.dtype != part.dtype or b > self._peer.max_batch:
+                # Collective set-up: every rank reaches it at the same call
+                # (the same metadata on every rank).
+                if self._peer is not None:
+                    self._peer.close()
+                self._peer = PeerHeadGather(self.group, max(b, self.max_batch), hq_local, d, part.dtype,
+                                            part.device)
+            if out is None:
+                out = torch.empty((b, self.hq, d), dtype=part.dtype, device=part.device)
+            return self._peer(part, out)
         gathered = torch.empty((self.world, b, hq_local, d), dtype=part.dtype, device=part.device)
         if self._nccl:
             dist.all_gather_into_tensor(gathered, part.contiguous(), group=self.group)
@@ -104,3 +223,14 @@ class HeadShardedDecode:
             return full
         out.copy_(full)
         return out
+
+    def check(self) -> None:
+        """Raise PagedAttentionError if a peer wait gave up (synchronises)."""
+        if self._peer is not None:
+            self._peer.check()
+
+    def close(self) -> None:
+        """Release the peer mappings (collective)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None

@@ -90,3 +90,30 @@ def test_unsupported_dtype():
     fake = ctypes.c_void_p(16)
     assert lib.pa_kv_scatter(fake, 0, 0, 0, fake, 0, 0, 0, 0, fake, 1, 4, fake, fake, 64, 2, 64, 3, None) == \
         _lib.PA_ERR_UNSUPPORTED
+
+
+def test_peer_gather_sizes_and_host_checks():
+    lib = _lib.load()
+    # Header + 2 slots x world x slice (slices rounded to 16 bytes).
+    assert lib.pa_peer_gather_bytes(2, 7168) == 256 + 2 * 2 * 7168
+    assert lib.pa_peer_gather_bytes(1, 10) == 256 + 2 * 16
+    assert lib.pa_peer_gather_bytes(0, 64) == 0
+    assert lib.pa_peer_gather_bytes(_lib.PA_PEER_MAX_RANKS + 1, 64) == 0
+    fake = ctypes.c_void_p(4096)
+    areas = (ctypes.c_void_p * 2)(4096, 8192)
+    ok = dict(p_s0=7 * 64, p_s1=64, batch=8, hl=7, d=64, dt=2, rank=0, world=2, nbytes=1 << 20, o_s0=14 * 64,
+              o_s1=64, limit=0)
+
+    def call(**kw):
+        a = {**ok, **kw}
+        return lib.pa_head_allgather(fake, a["p_s0"], a["p_s1"], a["batch"], a["hl"], a["d"], a["dt"], a["rank"],
+                                     a["world"], areas, a["nbytes"], fake, a["o_s0"], a["o_s1"], a["limit"], None)
+
+    assert call(rank=2) == _lib.PA_ERR_INVALID              # rank outside the world
+    assert call(world=0) == _lib.PA_ERR_INVALID
+    assert call(d=4) == _lib.PA_ERR_INVALID                 # a head row of 8 bytes is not 16-byte vectors
+    assert call(o_s1=60) == _lib.PA_ERR_INVALID             # unaligned stride
+    assert call(limit=-1) == _lib.PA_ERR_INVALID
+    assert call(nbytes=256) == _lib.PA_ERR_CAPACITY         # area too small for two slots
+    assert lib.pa_ipc_export(None, None, None) == _lib.PA_ERR_INVALID
+    assert lib.pa_ipc_close(None) == _lib.PA_ERR_INVALID

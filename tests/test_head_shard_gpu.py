@@ -1,7 +1,8 @@
-"""KV-head-sharded decode on 2 GPUs over NCCL: each rank decodes its KV
-heads with the CUDA kernels and the all-gather of head outputs must rebuild
-the oracle's unsharded result (BF16 tolerance).  Needs two GPUs; skipped with
-fewer."""
+"""KV-head-sharded decode on 2 GPUs: each rank decodes its KV heads with the
+CUDA kernels, and the all-gather of head outputs, over NVLink peer stores
+(pa_head_allgather) and over NCCL, must rebuild the oracle's unsharded result
+(BF16 tolerance), bit-identically between the two transports, call after call
+and under CUDA-graph replay.  Needs two GPUs; skipped with fewer."""
 
 import os
 import socket
@@ -34,18 +35,45 @@ def _rank_main(rank, world, port, result_path):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     try:
         case = make_decode_case([4097, 30000, 17], 14, 2, 64, 16, torch.bfloat16, dev, seed=21)
-        hs = HeadShardedDecode(14, 2)
-        out = hs(hs.local_queries(case["q"]), shard_pool(case["k"], hs.kv_slice), shard_pool(case["v"], hs.kv_slice),
-                 case["tables"], case["lens"], 16)
         q, k, v, tables, lens = case["np"]
-        ref = O.decode_batch(q, k, v, tables, lens, 16)
-        err = (out.float().cpu() - torch.from_numpy(ref)).abs()
-        ok = bool(torch.isfinite(out.float()).all()) and bool((err <= 2e-2 + 1e-2 * torch.from_numpy(ref).abs()).all())
+        ref = torch.from_numpy(O.decode_batch(q, k, v, tables, lens, 16))
+        checks, outs = {}, {}
+        for transport in ("peer", "collective"):
+            hs = HeadShardedDecode(14, 2, transport=transport, max_batch=4)
+            ql = hs.local_queries(case["q"])
+            kl, vl = shard_pool(case["k"], hs.kv_slice), shard_pool(case["v"], hs.kv_slice)
+            for _ in range(3):  # the exchange alternates its two slots call by call
+                out = hs(ql, kl, vl, case["tables"], case["lens"], 16)
+            torch.cuda.synchronize()
+            hs.check()
+            err = (out.float().cpu() - ref).abs()
+            checks[transport] = bool(torch.isfinite(out.float()).all()) and bool((err <= 2e-2 + 1e-2 * ref.abs()).all())
+            outs[transport] = out
+            if transport == "peer":
+                # Replays of a captured call keep the ranks in step: the call
+                # number lives in device memory.
+                s = torch.cuda.Stream(dev)
+                s.wait_stream(torch.cuda.current_stream())
+                out_g = torch.empty_like(out)
+                with torch.cuda.stream(s):
+                    hs(ql, kl, vl, case["tables"], case["lens"], 16, out=out_g)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=s):
+                    hs(ql, kl, vl, case["tables"], case["lens"], 16, out=out_g)
+                out_g.zero_()
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize()
+                hs.check()
+                checks["graph"] = torch.equal(out_g, out)
+                del graph
+            hs.close()
+        checks["peer == collective"] = torch.equal(outs["peer"], outs["collective"])
         flags = [None] * world
-        dist.all_gather_object(flags, ok)
+        dist.all_gather_object(flags, checks)
         if rank == 0:
             with open(result_path, "w") as f:
-                f.write("ok" if all(flags) else f"mismatch {flags}")
+                f.write("ok" if all(all(c.values()) for c in flags) else f"mismatch {flags}")
     finally:
         dist.destroy_process_group()
 

@@ -1,0 +1,76 @@
+"""pa_head_allgather on one GPU, through the C ABI: the one-rank exchange
+copies the slice into the output call after call, and a wait for a peer flag
+that nothing raises gives up after its limit with PA_DEVICE_TIMEOUT_PEER in
+the area's status word, without a fault or a hang (the two-GPU exchange is in
+test_head_shard_gpu.py)."""
+
+import ctypes
+
+import pytest
+import torch
+
+from mini_llm_runtime_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _call(lib, part, out, areas, nbytes, rank, world, limit_ns=0):
+    arr = (ctypes.c_void_p * world)(*[a.data_ptr() for a in areas])
+    b, hl, d = part.shape
+    return lib.pa_head_allgather(part.data_ptr(), part.stride(0), part.stride(1), b, hl, d,
+                                 _lib.dtype_code(part.dtype), rank, world, arr, nbytes, out.data_ptr(),
+                                 out.stride(0), out.stride(1), limit_ns,
+                                 torch.cuda.current_stream().cuda_stream)
+
+
+def test_one_rank_copies_every_call(cuda_device):
+    lib = _lib.load()
+    b, hl, d = 8, 7, 64
+    nbytes = lib.pa_peer_gather_bytes(1, b * hl * d * 2)
+    area = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    for i in range(3):
+        part = torch.randn(b, hl, d, device=cuda_device).to(torch.bfloat16)
+        out = torch.full((b, hl, d), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+        assert _call(lib, part, out, [area], nbytes, 0, 1) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, part)
+        words = area[128:140].view(torch.int32).tolist()
+        assert words == [0, i + 1, 0]  # arrivals rewound, calls counted, status clear
+
+
+def test_strided_part_and_output(cuda_device):
+    lib = _lib.load()
+    b, hl, d = 5, 3, 128
+    nbytes = lib.pa_peer_gather_bytes(1, b * hl * d * 4)
+    area = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    big = torch.randn(b, 2 * hl, d, device=cuda_device)
+    part = big[:, 1::2]  # head stride 2 * d
+    out_big = torch.zeros(b, hl + 2, d, device=cuda_device)
+    out = out_big[:, 1:1 + hl]
+    assert _call(lib, part, out, [area], nbytes, 0, 1) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out, part)
+    assert torch.count_nonzero(out_big[:, 0]) == 0 and torch.count_nonzero(out_big[:, -1]) == 0
+
+
+def test_missing_peer_times_out_with_status(cuda_device):
+    # Two ranks, both slots pointing at this GPU's own area: the kernel raises
+    # "rank 0"'s flag and waits for "rank 1"'s, which nothing raises.
+    lib = _lib.load()
+    b, hl, d = 4, 7, 64
+    nbytes = lib.pa_peer_gather_bytes(2, b * hl * d * 2)
+    area = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    part = torch.randn(b, hl, d, device=cuda_device).to(torch.bfloat16)
+    out = torch.zeros(b, 2 * hl, d, device=cuda_device, dtype=torch.bfloat16)
+    assert _call(lib, part, out, [area, area], nbytes, 0, 2, limit_ns=20_000_000) == 0
+    torch.cuda.synchronize()
+    assert area[136:140].view(torch.int32).item() == _lib.PA_DEVICE_TIMEOUT_PEER
+    assert torch.equal(out[:, :hl], part)  # this rank's heads landed; the peer's did not
+    assert torch.count_nonzero(out[:, hl:]) == 0
+    # Re-zeroed, the area serves normal calls again.
+    area.zero_()
+    one = torch.zeros(b, hl, d, device=cuda_device, dtype=torch.bfloat16)
+    assert _call(lib, part, one, [area], lib.pa_peer_gather_bytes(1, b * hl * d * 2), 0, 1) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(one, part)
+    assert area[136:140].view(torch.int32).item() == 0
