@@ -603,7 +603,7 @@ def run_head_shard(args, rank, world, local_rank):
     """Config 3 (8 x 32,768 tokens, 14/2 heads) decoded with its KV heads split
     over the ranks: each rank streams its heads' KV from its own pools and one
     all-gather per layer rebuilds [B, Hq, D].  The all-gather runs two ways:
-    pa_head_allgather (peer stores over NVLink and a flag handshake, the
+    pa_head_allgather (peer stores over NVLink of self-validating lines, the
     default `transport="peer"`) and NCCL's all_gather_into_tensor.  Layers x
     (decode + all-gather) are captured in one CUDA graph; `value` is the whole
     batch's algorithmic KV bytes per second with the peer all-gather (max over
@@ -687,7 +687,7 @@ def run_head_shard(args, rank, world, local_rank):
             "mode": "head-shard", "metric": METRIC, "value": kv / (peer["step"] * 1e-3) / 1e9, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
             "data": "synthetic", "ms_per_layer": peer["step"], "allgather_ms_per_layer": peer["gather"],
-            "transport": "pa_head_allgather: peer stores over NVLink + flag handshake, one kernel per layer",
+            "transport": "pa_head_allgather: peer stores over NVLink of lines carrying the call number, one kernel per layer",
             "nccl": {"value": kv / (coll["step"] * 1e-3) / 1e9, "ms_per_layer": coll["step"],
                      "allgather_ms_per_layer": coll["gather"]},
             "config": {"workload": "config3: 8 x 32768 tokens, 14/2 heads, D64, bs16, KV heads split over the "

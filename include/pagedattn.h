@@ -376,16 +376,17 @@ PA_API int pa_accumulate_pv(const float* p, const float* v, float* out, int64_t 
  * pa_head_allgather: part [batch, heads_local, head_dim] with element strides
  * (p_s0, p_s1); out [batch, world*heads_local, head_dim] with (o_s0, o_s1);
  * dtype F16/BF16/F32 (head_dim * esize, strides and pointers 16-byte
- * aligned).  One kernel stores `part` into `out` and into every peer's area,
- * raises this rank's flag in every peer's area (system-scope release), waits
- * until every peer's flag reaches this call's number (bounded: wait_limit_ns,
+ * aligned).  One kernel (launched with programmatic dependent launch) stores
+ * `part` into `out` and, as 16-byte lines that carry 8 data bytes and the
+ * call's number twice, into every peer's area; it then polls its own area
+ * until every peer's lines of this call have arrived (bounded: wait_limit_ns,
  * 0 = 500 ms; on expiry the area's status word at byte 136 becomes
- * PA_DEVICE_TIMEOUT_PEER and `out` keeps only this rank's heads), then copies
- * the peers' heads into `out`.  Every rank must make the same sequence of
- * calls; calls on one rank must be ordered on one stream.  CUDA-graph capture
- * works: the call number lives in the area, not in the launch arguments.
- * After a timeout the exchange is out of step: zero the areas on every rank
- * (between a host barrier and the next call) before reusing them.
+ * PA_DEVICE_TIMEOUT_PEER and `out` keeps only the heads that arrived) and
+ * decodes them into `out`.  Every rank must make the same sequence of calls;
+ * calls on one rank must be ordered on one stream.  CUDA-graph capture works:
+ * the call number lives in the area, not in the launch arguments.  After a
+ * timeout the exchange is out of step: zero the areas on every rank (between
+ * a host barrier and the next call) before reusing them.
  */
 PA_API size_t pa_peer_gather_bytes(int world, int64_t slice_bytes);
 PA_API int pa_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out);

@@ -2,25 +2,28 @@
 // sharded by KV head (rank r of g decodes query heads [r*Hq/g, (r+1)*Hq/g)
 // of every sequence and every rank needs all Hq heads).
 //
-// One kernel does the exchange: every rank stores its [B, Hq/g, D] slice
-// straight into each peer's exchange area (plain 16-byte stores through a
-// CUDA IPC mapping of the peer's memory), raises its flag in each peer's area
-// with a system-scope release, waits (bounded) until every peer's flag has
-// reached this call's number, and copies the peers' slices into its
-// [B, Hq, D] output.  The slice is a few KB per layer, so the exchange is
-// latency-bound: one launch and one NVLink round trip instead of a
-// collective library call.
+// One kernel does the exchange, in the "low-latency" line format: every
+// 16-byte store carries 8 bytes of data and the call's number twice
+// ({w0, n, w1, n}), so a receiver knows a line has arrived when both number
+// words read n; no fence, flag or second round trip is needed.  Each rank
+// stores its [B, Hq/g, D] slice, so encoded, straight into every peer's
+// exchange area (16-byte stores through a CUDA IPC mapping of the peer's
+// memory), copies it into its own [B, Hq, D] output, then polls its own area
+// (bounded) for the peers' lines and decodes them into the output.  The
+// slice is a few KB per layer: the exchange is latency-bound, one launch and
+// one NVLink crossing.
 //
 // Exchange area of each rank (one device allocation, mapped on every peer):
-//   [0, 128)     uint32 flag[r]: the number of the last call whose slice rank
-//                r has stored here (written by rank r only)
-//   [128, 256)   uint32 arrivals (CTAs of the current call that finished
-//                their stores), uint32 calls (calls completed), int status
+//   [0, 128)     reserved
+//   [128, 256)   uint32 arrivals (CTAs of the current call past their
+//                stores), uint32 calls (calls made), int status
 //                (PA_DEVICE_TIMEOUT_PEER after a wait gave up); local use
-//   [256, ...)   2 slots x world x slice bytes; call n uses slot n & 1, so a
-//                peer that runs one call ahead writes the other slot.
-// A peer can run at most one call ahead: its next call signals only after it
-// has seen this rank's flag for the current one.
+//   [256, ...)   2 slots x world x 2 * slice bytes of lines; call n uses slot
+//                n & 1, so a peer that runs one call ahead writes the other
+//                slot, and a line left from call n - 2 reads as not arrived.
+// A peer can run at most one call ahead: it finishes a call only after it
+// has received this rank's lines of that call, which this rank stores only
+// after it has finished the call before.
 #include <cstring>
 #include <mutex>
 
@@ -45,15 +48,17 @@ struct GatherParams {
   uint64_t limit_ns;
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void st_line(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
 }
-
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ uint4 ld_line(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
 }
 
 __global__ void __launch_bounds__(kGatherThreads) head_allgather_kernel(GatherParams p) {
@@ -67,76 +72,58 @@ __global__ void __launch_bounds__(kGatherThreads) head_allgather_kernel(GatherPa
   uint32_t* calls = arrivals + 1;
   int* status = reinterpret_cast<int*>(mine + 136);
   __shared__ uint32_t call_s;
-  __shared__ int ok_s;
   if (threadIdx.x == 0) call_s = *reinterpret_cast<volatile uint32_t*>(calls) + 1u;
   __syncthreads();
-  const uint32_t call = call_s;
-  const int64_t slot_off = kAreaHeader + (int64_t)(call & 1u) * p.world * p.slice_bytes;
-  const int64_t units = (int64_t)p.B * p.hl * p.row_vecs;
+  const uint32_t n = call_s;
+  const int64_t lines_per_rank = 2 * p.slice_bytes;  // bytes of lines per rank's slice
+  const int64_t slot_off = kAreaHeader + (int64_t)(n & 1u) * p.world * lines_per_rank;
+  const int64_t units = (int64_t)p.B * p.hl * p.row_vecs;  // 16-byte data vectors of a slice
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
 
-  // This rank's slice: into its own output and into every peer's area.
+  // This rank's slice: into its own output, and as lines into every peer's area.
   for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += stride) {
     const int64_t row = u / p.row_vecs;
     const int v = static_cast<int>(u - row * p.row_vecs);
     const int b = static_cast<int>(row / p.hl), h = static_cast<int>(row - (int64_t)b * p.hl);
     const int4 val = *reinterpret_cast<const int4*>(p.part + b * p.p_s0 + h * p.p_s1 + v * 16);
     *reinterpret_cast<int4*>(p.out + b * p.o_s0 + (int64_t)(p.rank * p.hl + h) * p.o_s1 + v * 16) = val;
-    for (int q = 0; q < p.world; ++q)
-      if (q != p.rank)
-        *reinterpret_cast<int4*>(p.areas[q] + slot_off + p.rank * p.slice_bytes + u * 16) = val;
+    for (int q = 0; q < p.world; ++q) {
+      if (q == p.rank) continue;
+      uint8_t* line = p.areas[q] + slot_off + p.rank * lines_per_rank + u * 32;
+      st_line(line, (uint32_t)val.x, n, (uint32_t)val.y, n);
+      st_line(line + 16, (uint32_t)val.z, n, (uint32_t)val.w, n);
+    }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    // The CTA barrier orders every thread's stores before thread 0's; with
-    // several CTAs a counter (GPU scope) orders them before the last CTA's.
-    // The last CTA then releases them at system scope (fence.acq_rel.sys is
-    // cumulative over what it has observed) and raises this rank's flag in
-    // every peer's area.
-    bool last = true;
-    if (gridDim.x > 1) {
-      __threadfence();
-      last = atomicAdd(arrivals, 1u) == gridDim.x - 1;
-      if (last) {
-        __threadfence();
-        *reinterpret_cast<volatile uint32_t*>(arrivals) = 0u;
-      }
-    }
-    if (last) {
-      fence_acq_rel_sys();
-      for (int q = 0; q < p.world; ++q)
-        if (q != p.rank) st_relaxed_sys(reinterpret_cast<uint32_t*>(p.areas[q]) + p.rank, call);
-      *reinterpret_cast<volatile uint32_t*>(calls) = call;
-    }
-    // Wait (bounded) until every peer has stored its slice of this call.
-    int ok = 1;
-    const uint32_t* flag = reinterpret_cast<const uint32_t*>(mine);
-    const uint64_t t0 = globaltimer_ns();
-    for (int r = 0; r < p.world && ok; ++r) {
-      if (r == p.rank) continue;
+  // The call counter advances once every CTA has read it.
+  if (threadIdx.x == 0 && atomicAdd(arrivals, 1u) == gridDim.x - 1) {
+    *reinterpret_cast<volatile uint32_t*>(arrivals) = 0u;
+    *reinterpret_cast<volatile uint32_t*>(calls) = n;
+  }
+  // The peers' lines, polled (bounded) and decoded into the output.
+  const uint8_t* slot = mine + slot_off;
+  const uint64_t t0 = globaltimer_ns();
+  bool ok = true;
+  for (int r = 0; r < p.world && ok; ++r) {
+    if (r == p.rank) continue;
+    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units && ok; u += stride) {
+      const uint8_t* line = slot + r * lines_per_rank + u * 32;
+      uint4 a, c;
       for (uint32_t i = 0;; ++i) {
-        if (static_cast<int32_t>(ld_acquire_sys(flag + r) - call) >= 0) break;
+        a = ld_line(line);
+        c = ld_line(line + 16);
+        if (a.y == n && a.w == n && c.y == n && c.w == n) break;
         if ((i & 63) == 63 && globaltimer_ns() - t0 > p.limit_ns) {
           record_status(status, PA_DEVICE_TIMEOUT_PEER);
-          ok = 0;
+          ok = false;
           break;
         }
       }
-    }
-    ok_s = ok;
-  }
-  __syncthreads();
-  if (!ok_s) return;
-  // The peers' slices, from this rank's area into its output.
-  const uint8_t* slot = mine + slot_off;
-  for (int r = 0; r < p.world; ++r) {
-    if (r == p.rank) continue;
-    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += stride) {
+      if (!ok) break;
       const int64_t row = u / p.row_vecs;
       const int v = static_cast<int>(u - row * p.row_vecs);
       const int b = static_cast<int>(row / p.hl), h = static_cast<int>(row - (int64_t)b * p.hl);
-      const int4 val = __ldcg(reinterpret_cast<const int4*>(slot + r * p.slice_bytes + u * 16));
-      *reinterpret_cast<int4*>(p.out + b * p.o_s0 + (int64_t)(r * p.hl + h) * p.o_s1 + v * 16) = val;
+      *reinterpret_cast<int4*>(p.out + b * p.o_s0 + (int64_t)(r * p.hl + h) * p.o_s1 + v * 16) =
+          make_int4((int)a.x, (int)a.z, (int)c.x, (int)c.z);
     }
   }
 }
@@ -161,7 +148,8 @@ AddressRangeFn get_address_range() {
 
 extern "C" size_t pa_peer_gather_bytes(int world, int64_t slice_bytes) {
   if (world < 1 || world > PA_PEER_MAX_RANKS || slice_bytes < 0) return 0;
-  return static_cast<size_t>(pa::kAreaHeader + 2 * (int64_t)world * ((slice_bytes + 15) / 16 * 16));
+  // Two slots of lines: 32 bytes of lines per 16 bytes of data.
+  return static_cast<size_t>(pa::kAreaHeader + 2 * (int64_t)world * 2 * ((slice_bytes + 15) / 16 * 16));
 }
 
 extern "C" int pa_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out) {

@@ -15,8 +15,8 @@ the collective is latency-bound, not bandwidth-bound.
 This is the one place an exchange between GPUs sits on the path.  By default
 (``transport="peer"`` on CUDA ranks) it is ``pa_head_allgather``: one kernel
 stores each rank's slice straight into every peer's memory over NVLink (CUDA
-IPC mappings set up once), raises a flag there, and waits (bounded) for the
-peers' flags: one launch and one NVLink round trip per layer.
+IPC mappings set up once) as lines that carry the call's number, and polls
+(bounded) for the peers' lines: one launch and one NVLink crossing per layer.
 ``transport="collective"`` runs ``torch.distributed`` all-gather instead (NCCL
 on GPUs, gloo on CPU ranks).  The reference runs one process on one device
 (runtime/model_runner.py:146-288), so it has no counterpart; the per-rank math

@@ -94,9 +94,9 @@ def test_unsupported_dtype():
 
 def test_peer_gather_sizes_and_host_checks():
     lib = _lib.load()
-    # Header + 2 slots x world x slice (slices rounded to 16 bytes).
-    assert lib.pa_peer_gather_bytes(2, 7168) == 256 + 2 * 2 * 7168
-    assert lib.pa_peer_gather_bytes(1, 10) == 256 + 2 * 16
+    # Header + 2 slots x world x lines (32 bytes of lines per 16 data bytes).
+    assert lib.pa_peer_gather_bytes(2, 7168) == 256 + 2 * 2 * 2 * 7168
+    assert lib.pa_peer_gather_bytes(1, 10) == 256 + 2 * 2 * 16
     assert lib.pa_peer_gather_bytes(0, 64) == 0
     assert lib.pa_peer_gather_bytes(_lib.PA_PEER_MAX_RANKS + 1, 64) == 0
     fake = ctypes.c_void_p(4096)

@@ -1,8 +1,8 @@
 """pa_head_allgather on one GPU, through the C ABI: the one-rank exchange
-copies the slice into the output call after call, and a wait for a peer flag
-that nothing raises gives up after its limit with PA_DEVICE_TIMEOUT_PEER in
-the area's status word, without a fault or a hang (the two-GPU exchange is in
-test_head_shard_gpu.py)."""
+copies the slice into the output call after call, and a wait for a peer's
+lines that nothing stores gives up after its limit with PA_DEVICE_TIMEOUT_PEER
+in the area's status word, without a fault or a hang (the two-GPU exchange is
+in test_head_shard_gpu.py)."""
 
 import ctypes
 
@@ -54,8 +54,8 @@ def test_strided_part_and_output(cuda_device):
 
 
 def test_missing_peer_times_out_with_status(cuda_device):
-    # Two ranks, both slots pointing at this GPU's own area: the kernel raises
-    # "rank 0"'s flag and waits for "rank 1"'s, which nothing raises.
+    # Two ranks, both pointing at this GPU's own area: the kernel stores "rank
+    # 0"'s lines and polls for "rank 1"'s, which nothing stores.
     lib = _lib.load()
     b, hl, d = 4, 7, 64
     nbytes = lib.pa_peer_gather_bytes(2, b * hl * d * 2)
