@@ -635,8 +635,8 @@ def run_head_shard(args, rank, world, local_rank):
     s = torch.cuda.Stream(device)
     s.wait_stream(torch.cuda.current_stream())
 
-    def measure(transport: str) -> dict:
-        hs = HeadShardedDecode(HQ, HKV, transport=transport, max_batch=len(ctx))
+    def measure(transport: str, fuse: bool = True) -> dict:
+        hs = HeadShardedDecode(HQ, HKV, transport=transport, max_batch=len(ctx), fuse=fuse)
 
         def body(gather_only=False):
             for l in range(layers):
@@ -679,6 +679,7 @@ def run_head_shard(args, rank, world, local_rank):
         return r
 
     peer = measure("peer")
+    unfused = measure("peer", fuse=False)
     coll = measure("collective")
     torch.cuda.synchronize()
     kv = int(ctx.sum()) * HKV * D * 2 * 2
@@ -686,8 +687,12 @@ def run_head_shard(args, rank, world, local_rank):
         print(json.dumps({
             "mode": "head-shard", "metric": METRIC, "value": kv / (peer["step"] * 1e-3) / 1e9, "unit": UNIT,
             "n_gpus": world, "steps": args.steps, "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
-            "data": "synthetic", "ms_per_layer": peer["step"], "allgather_ms_per_layer": peer["gather"],
-            "transport": "pa_head_allgather: peer stores over NVLink of lines carrying the call number, one kernel per layer",
+            "data": "synthetic", "ms_per_layer": peer["step"],
+            "transport": "pa_paged_decode_allgather: the decode's merge kernel stores its output rows into the "
+                         "peers' memory over NVLink as lines carrying the call number and polls for theirs",
+            "unfused": {"value": kv / (unfused["step"] * 1e-3) / 1e9, "ms_per_layer": unfused["step"],
+                        "allgather_ms_per_layer": unfused["gather"],
+                        "transport": "decode, then pa_head_allgather (a kernel of its own)"},
             "nccl": {"value": kv / (coll["step"] * 1e-3) / 1e9, "ms_per_layer": coll["step"],
                      "allgather_ms_per_layer": coll["gather"]},
             "config": {"workload": "config3: 8 x 32768 tokens, 14/2 heads, D64, bs16, KV heads split over the "

@@ -396,6 +396,45 @@ PA_API int pa_head_allgather(const void* part, int64_t p_s0, int64_t p_s1, int b
                              int dtype, int rank, int world, void* const* areas, int64_t area_bytes, void* out,
                              int64_t o_s0, int64_t o_s1, int64_t wait_limit_ns, void* stream);
 
+/*
+ * Batched decode with the all-gather of head outputs fused into it, for
+ * decode sharded by KV head across `world` GPUs of one node (the exchange of
+ * pa_head_allgather, done by the decode's own merge kernel: each of its CTAs
+ * stores its finished output rows into every peer's exchange area and polls
+ * its own area for the peers' rows of the same sequence and heads).
+ *
+ * Replaces, on the KV-head-sharded path, paged_attention_decode_batch_parallel
+ * (kernels/reference/paged_attention.py:178-254) on this rank's heads
+ * followed by an all-gather; the reference has no multi-GPU decode.
+ *
+ * Arguments as pa_paged_decode_ex (partition_tokens 0; new_k / new_v /
+ * slot_mapping all null, or all set for the fused KV write), with `out`
+ * pointing at THIS rank's first head inside the [batch, world * num_q_heads,
+ * head_dim] output of all ranks (strides o_s0, o_s1 of that tensor): rank q's
+ * heads are written num_q_heads * (q - rank) heads away.  num_q_heads and
+ * num_kv_heads are this rank's.  `areas` is the host array of every rank's
+ * exchange area (see pa_head_allgather; the two share the areas and their
+ * call number), each of at least pa_decode_allgather_bytes(...) bytes.  On
+ * expiry of a wait (wait_limit_ns, 0 = 500 ms) PA_DEVICE_TIMEOUT_PEER goes to
+ * the area's status word and the workspace status word.
+ *
+ * Returns PA_ERR_UNSUPPORTED, with nothing launched, when the call cannot
+ * take the balanced kernel (F32, head_dim other than 64/128, batch > 1024,
+ * unaligned views) or when the merge kernel's grid does not fit on the device
+ * at once (every CTA waits for its peers, so all must be resident): the
+ * caller then decodes with pa_paged_decode_ex and exchanges with
+ * pa_head_allgather.  Every rank must make the same sequence of calls.
+ */
+PA_API size_t pa_decode_allgather_bytes(int batch, int num_kv_heads, int num_q_heads, int head_dim, int world);
+PA_API int pa_paged_decode_allgather(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k, const void* new_v,
+                                     const int64_t* slot_mapping, void* k_pool_layer, void* v_pool_layer,
+                                     int64_t num_blocks, int block_size, int num_kv_heads, int head_dim,
+                                     const int64_t* block_tables, int64_t bt_stride, int64_t bt_width,
+                                     const int64_t* context_lens, void* out, int64_t o_s0, int64_t o_s1, int batch,
+                                     int num_q_heads, float scale, int dtype, int flags, int rank, int world,
+                                     void* const* areas, int64_t area_bytes, int64_t wait_limit_ns, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -105,6 +105,13 @@ SIGNATURES: dict[str, tuple] = {
     "pa_ipc_export": (_i32, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
     "pa_ipc_import": (_i32, [_c_void_p, ctypes.c_uint64, ctypes.POINTER(_c_void_p), ctypes.POINTER(_c_void_p)]),
     "pa_ipc_close": (_i32, [_c_void_p]),
+    "pa_decode_allgather_bytes": (_size, [_i32, _i32, _i32, _i32, _i32]),
+    "pa_paged_decode_allgather": (
+        _i32,
+        [_c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i32, _i32, _i32,
+         _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64, _i32, _i32, _f32, _i32, _i32, _i32, _i32,
+         ctypes.POINTER(_c_void_p), _i64, _i64, _c_void_p, _size, _c_void_p],
+    ),
     "pa_head_allgather": (
         _i32,
         [_c_void_p, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, ctypes.POINTER(_c_void_p), _i64, _c_void_p,

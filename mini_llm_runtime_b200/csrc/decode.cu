@@ -418,13 +418,33 @@ struct WarpState {
 
 // Eight outputs of one row as a single 16-byte store.
 template <typename T>
-__device__ __forceinline__ void store8(T* dst, const float* v, float scale) {
+__device__ __forceinline__ int4 pack8(const float* v, float scale) {
   int4 pk;
   pk.x = static_cast<int>(MmaOp<T>::pack(v[0] * scale, v[1] * scale));
   pk.y = static_cast<int>(MmaOp<T>::pack(v[2] * scale, v[3] * scale));
   pk.z = static_cast<int>(MmaOp<T>::pack(v[4] * scale, v[5] * scale));
   pk.w = static_cast<int>(MmaOp<T>::pack(v[6] * scale, v[7] * scale));
-  *reinterpret_cast<int4*>(dst) = pk;
+  return pk;
+}
+template <typename T>
+__device__ __forceinline__ void store8(T* dst, const float* v, float scale) {
+  *reinterpret_cast<int4*>(dst) = pack8<T>(v, scale);
+}
+
+// Lines of the peer exchange: 8 data bytes and the call number twice per
+// 16-byte store, so a line read back with both numbers equal to the call's
+// has arrived whole (each 8-byte half lands atomically).
+__device__ __forceinline__ void st_line(void* ptr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_line(const void* ptr) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(ptr)
+               : "memory");
+  return v;
 }
 
 // acc[0..8) += wt * (v0, v1).
@@ -474,6 +494,14 @@ struct FlatParams {
   void* k_pool;
   void* v_pool;
   int64_t num_slots;
+  // Head all-gather fused into the combine (xworld 0: none): `out` points at
+  // this rank's first head inside the [B, xworld * Hq, D] output of all
+  // ranks; rank q's heads start Hq * (q - xrank) heads away.  xareas are the
+  // ranks' exchange areas (pa_head_allgather's layout), this rank's at xrank.
+  uint8_t* xareas[PA_PEER_MAX_RANKS];
+  int xrank, xworld;
+  int64_t xline_bytes;  // bytes of lines per rank and slot: B * SPS * 16 * (D / 8) * 32
+  uint64_t xlimit_ns;
 };
 
 // A segment's place in the index space.
@@ -908,7 +936,7 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
 // records of one item are split over several threads (stripes).
 constexpr int kCombineThreads = 64;
 
-template <typename T, int D, int PK, int ROWS>
+template <typename T, int D, int PK, int ROWS, bool XCHG = false>
 __global__ void __launch_bounds__(kCombineThreads, 8) decode_combine_kernel(FlatParams p) {
   constexpr int kRec = D + 4;
   constexpr int kCombineRows = ROWS;
@@ -918,6 +946,7 @@ __global__ void __launch_bounds__(kCombineThreads, 8) decode_combine_kernel(Flat
   __shared__ float sm_m[kCombineThreads], sm_l[kCombineThreads];
   __shared__ float4 sm_acc[kCombineThreads][2];
   __shared__ int wsum[2][kCombineThreads / 32];
+  __shared__ uint32_t call_s;
   const int tid = threadIdx.x;
   const int sid = blockIdx.x;
   const int b = sid / p.SPS, segx = sid - b * p.SPS;
@@ -950,22 +979,29 @@ __global__ void __launch_bounds__(kCombineThreads, 8) decode_combine_kernel(Flat
   int64_t ctx = p.context_lens[b];
   ctx = ctx > cap ? cap : ctx;
   const int nsub = ctx > 0 ? static_cast<int>((ctx + kSub - 1) / kSub) : 0;
-  if (nsub == 0) return;
+  // With the exchange every CTA takes part to the end (its rows go to the
+  // peers, and it counts in for the call number); otherwise a CTA without
+  // rows to merge returns at once.
+  if (!XCHG && nsub == 0) return;
   const int64_t total = (int64_t)all * p.SPS;
   const int G = static_cast<int>(total < (int64_t)p.grid ? total : (int64_t)p.grid);
   const int64_t start = (int64_t)before * p.SPS + (int64_t)segx * nsub, end = start + nsub;
   auto cta_of = [&](int64_t xx) { return static_cast<int>(((xx + 1) * G - 1) / total); };
-  const int c0 = cta_of(start), c1 = cta_of(end - 1);
-  if (c0 == c1) return;  // finished inside one CTA of the main kernel
+  const int c0 = nsub > 0 ? cta_of(start) : 0, c1 = nsub > 0 ? cta_of(end - 1) : 0;
+  const bool merged_here = nsub > 0 && c0 != c1;  // else the main kernel finished it inside one CTA
+  if (!XCHG && !merged_here) return;
   int kvh0, h0, hn;
   seg_heads<PK>(p, segx, kvh0, h0, hn);
   const int item = tid % kItems, stripe = tid / kItems;
   const int r = blockIdx.y * kCombineRows + item / (D / 8), d = 8 * (item % (D / 8));
   const int hh = row_head<PK>(r, p.group, hn);
-  grid_dep_wait();  // the main kernel's records are complete and visible
+  grid_dep_wait();  // the main kernel's records (and outputs) are complete and visible
+  if constexpr (XCHG) {
+    if (tid == 0) call_s = *reinterpret_cast<volatile uint32_t*>(p.xareas[p.xrank] + 132) + 1u;
+  }
   float mrun = -INFINITY, lrun = 0.f;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  if (hh >= 0) {
+  if (merged_here && hh >= 0) {
     for (int cb = c0 + stripe; cb <= c1; cb += 8 * kStripes) {  // eight records' loads in flight
       float2 ml[8];
       float4 v0[8], v1[8];
@@ -1007,24 +1043,84 @@ __global__ void __launch_bounds__(kCombineThreads, 8) decode_combine_kernel(Flat
     sm_acc[tid][0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
     sm_acc[tid][1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     __syncthreads();
-    if (stripe != 0 || hh < 0) return;
-    float mx = -INFINITY;
+    if (!XCHG && (stripe != 0 || hh < 0)) return;
+    if (stripe == 0 && hh >= 0) {
+      float mx = -INFINITY;
 #pragma unroll
-    for (int s2 = 0; s2 < kStripes; ++s2) mx = fmaxf(mx, sm_m[s2 * kItems + item]);
-    lrun = 0.f;
+      for (int s2 = 0; s2 < kStripes; ++s2) mx = fmaxf(mx, sm_m[s2 * kItems + item]);
+      lrun = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
 #pragma unroll
-    for (int s2 = 0; s2 < kStripes; ++s2) {
-      const int t2 = s2 * kItems + item;
-      const float wt = exp2f(sm_m[t2] - mx);
-      lrun = fmaf(wt, sm_l[t2], lrun);
-      axpy8(wt, sm_acc[t2][0], sm_acc[t2][1], acc);
+      for (int s2 = 0; s2 < kStripes; ++s2) {
+        const int t2 = s2 * kItems + item;
+        const float wt = exp2f(sm_m[t2] - mx);
+        lrun = fmaf(wt, sm_l[t2], lrun);
+        axpy8(wt, sm_acc[t2][0], sm_acc[t2][1], acc);
+      }
     }
   }
-  if (hh < 0) return;
+  if (!XCHG && hh < 0) return;
   T* out = reinterpret_cast<T*>(p.out);
-  store8<T>(out + (int64_t)b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d, acc, p.out_scale / lrun);
+  T* dst = out + (int64_t)b * p.o_s0 + (int64_t)(h0 + hh) * p.o_s1 + d;
+  if constexpr (!XCHG) {
+    store8<T>(dst, acc, p.out_scale / lrun);
+  } else {
+    // This thread owns output (row r, columns d..d+7) of this rank's heads.
+    const bool own = nsub > 0 && hh >= 0 && stripe == 0;
+    int4 fin = make_int4(0, 0, 0, 0);
+    if (own) {
+      if (merged_here) {
+        fin = pack8<T>(acc, p.out_scale / lrun);
+        *reinterpret_cast<int4*>(dst) = fin;
+      } else {
+        fin = *reinterpret_cast<const int4*>(dst);  // written by the main kernel
+      }
+    }
+    __syncthreads();  // call_s
+    const uint32_t n = call_s;
+    const int64_t slot_off = 256 + (int64_t)(n & 1u) * p.xworld * p.xline_bytes;
+    const int64_t line = (((int64_t)sid * 16 + r) * (D / 8) + d / 8) * 32;
+    if (own) {
+      for (int q = 0; q < p.xworld; ++q) {
+        if (q == p.xrank) continue;
+        uint8_t* l = p.xareas[q] + slot_off + p.xrank * p.xline_bytes + line;
+        st_line(l, (uint32_t)fin.x, n, (uint32_t)fin.y, n);
+        st_line(l + 16, (uint32_t)fin.z, n, (uint32_t)fin.w, n);
+      }
+    }
+    __syncthreads();
+    uint8_t* mine = p.xareas[p.xrank];
+    uint32_t* arrivals = reinterpret_cast<uint32_t*>(mine + 128);
+    if (tid == 0 && atomicAdd(arrivals, 1u) == gridDim.x * gridDim.y - 1) {
+      *reinterpret_cast<volatile uint32_t*>(arrivals) = 0u;
+      *reinterpret_cast<volatile uint32_t*>(mine + 132) = n;
+    }
+    if (own) {
+      // The peers' rows of the same (segment, row, columns), polled (bounded).
+      const uint64_t t0 = globaltimer_ns();
+      for (int q = 0; q < p.xworld; ++q) {
+        if (q == p.xrank) continue;
+        const uint8_t* l = mine + slot_off + q * p.xline_bytes + line;
+        uint4 a, c;
+        bool got = true;
+        for (uint32_t i = 0;; ++i) {
+          a = ld_line(l);
+          c = ld_line(l + 16);
+          if (a.y == n && a.w == n && c.y == n && c.w == n) break;
+          if ((i & 63) == 63 && globaltimer_ns() - t0 > p.xlimit_ns) {
+            record_status(reinterpret_cast<int*>(mine + 136), PA_DEVICE_TIMEOUT_PEER);
+            record_status(p.status, PA_DEVICE_TIMEOUT_PEER);
+            got = false;
+            break;
+          }
+        }
+        if (!got) break;
+        *reinterpret_cast<int4*>(dst + (int64_t)(q - p.xrank) * p.Hq * p.o_s1) =
+            make_int4((int)a.x, (int)a.z, (int)c.x, (int)c.z);
+      }
+    }
+  }
 }
 
 // Merge `nw` warp records (m, l, O) of row h, column d (log2 domain).
@@ -1234,22 +1330,48 @@ bool set_smem_attr(K kern, size_t bytes, bool* done) {
   return true;
 }
 
+// Every CTA of an exchanging combine polls for its peers' rows, so all of its
+// CTAs must be resident at once: true when the grid fits the device's
+// occupancy for the kernel.
+template <typename K>
+bool fits_resident(K kern, int64_t ctas) {
+  static int per_sm[64] = {};
+  const int dev = current_device();
+  if (dev < 0 || dev >= 64) return false;
+  if (per_sm[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kCombineThreads, 0) != cudaSuccess || n <= 0)
+      return false;
+    per_sm[dev] = n;
+  }
+  return ctas <= (int64_t)per_sm[dev] * num_sms(dev);
+}
+
 template <typename T, int D, int PK, bool KV8>
 int launch_flat(const FlatParams& p, const CUtensorMap& tk, const CUtensorMap& tv, int grid, cudaStream_t st) {
   using S = FlatShape<D, PK, KV8>;
   using C = FlatCfg<D, PK, S::NW, S::ST, S::NSUB, KV8>;
   auto kern = decode_flat_kernel<T, D, PK, S::NW, S::ST, S::NSUB, kFlatCtasPerSm, KV8>;
+  // One item per thread (ROWS = 512 / D) unless segments span more than eight
+  // CTAs on average; then one row per CTA and the records go over stripes.
+  constexpr int kRowsWide = kCombineThreads * 8 / D;
+  const bool wide = (int64_t)grid <= 8 * (int64_t)p.B * p.SPS;
+  const dim3 cgrid(p.B * p.SPS, wide ? 16 / kRowsWide : 16);
+  if (p.xworld > 1) {
+    const int64_t ctas = (int64_t)cgrid.x * cgrid.y;
+    const bool ok = wide ? fits_resident(decode_combine_kernel<T, D, PK, kRowsWide, true>, ctas)
+                         : fits_resident(decode_combine_kernel<T, D, PK, 1, true>, ctas);
+    if (!ok) return PA_ERR_UNSUPPORTED;  // checked before anything is launched
+  }
   static bool done[64] = {};
   if (!set_smem_attr(kern, C::kSmem, done)) return PA_ERR_CUDA;
   const int r = launch_pdl(kern, dim3(grid), dim3(S::NW * 32), C::kSmem, st, tk, tv, p);
   if (r != PA_OK) return r;
-  // One item per thread (ROWS = 512 / D) unless segments span more than eight
-  // CTAs on average; then one row per CTA and the records go over stripes.
-  constexpr int kRowsWide = kCombineThreads * 8 / D;
-  if ((int64_t)grid > 8 * (int64_t)p.B * p.SPS)
-    return launch_pdl(decode_combine_kernel<T, D, PK, 1>, dim3(p.B * p.SPS, 16), dim3(kCombineThreads), 0, st, p);
-  return launch_pdl(decode_combine_kernel<T, D, PK, kRowsWide>, dim3(p.B * p.SPS, 16 / kRowsWide),
-                    dim3(kCombineThreads), 0, st, p);
+  if (p.xworld > 1)
+    return wide ? launch_pdl(decode_combine_kernel<T, D, PK, kRowsWide, true>, cgrid, dim3(kCombineThreads), 0, st, p)
+                : launch_pdl(decode_combine_kernel<T, D, PK, 1, true>, cgrid, dim3(kCombineThreads), 0, st, p);
+  if (!wide) return launch_pdl(decode_combine_kernel<T, D, PK, 1>, cgrid, dim3(kCombineThreads), 0, st, p);
+  return launch_pdl(decode_combine_kernel<T, D, PK, kRowsWide>, cgrid, dim3(kCombineThreads), 0, st, p);
 }
 
 template <typename T, int D>
@@ -1363,12 +1485,21 @@ struct FusedWrite {
   const int64_t* slots;
 };
 
+// Head all-gather fused into the decode (pa_paged_decode_allgather).
+struct Exchange {
+  int rank, world;
+  void* const* areas;
+  int64_t area_bytes;
+  int64_t wait_limit_ns;
+};
+
 int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_layer, const void* v_pool_layer,
                 int64_t num_blocks, int block_size, int num_kv_heads, int head_dim, const int64_t* block_tables,
                 int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
                 int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
                 void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused,
-                int flags = 0, int kv_dtype = -1, float k_scale = 1.f, float v_scale = 1.f);
+                int flags = 0, int kv_dtype = -1, float k_scale = 1.f, float v_scale = 1.f,
+                const Exchange* xc = nullptr);
 
 }  // namespace
 }  // namespace pa
@@ -1445,6 +1576,50 @@ extern "C" int pa_paged_decode_ex(const void* q, int64_t q_s0, int64_t q_s1, con
                                o_s0, o_s1, batch, num_q_heads, scale, dtype, workspace, workspace_bytes, stream);
 }
 
+extern "C" size_t pa_decode_allgather_bytes(int batch, int num_kv_heads, int num_q_heads, int head_dim,
+                                            int world) {
+  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0 ||
+      head_dim % 8 || world < 1 || world > PA_PEER_MAX_RANKS)
+    return 0;
+  const int group = num_q_heads / num_kv_heads;
+  const bool pk2 = pa::flat_pack2(num_q_heads, num_kv_heads);
+  const int sps = pk2 ? num_kv_heads / 2 : num_kv_heads * ((group + 15) / 16);
+  const int64_t lines = (int64_t)batch * sps * 16 * (head_dim / 8) * 32;
+  return static_cast<size_t>(256 + 2 * (int64_t)world * lines);
+}
+
+extern "C" int pa_paged_decode_allgather(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k,
+                                         const void* new_v, const int64_t* slot_mapping, void* k_pool_layer,
+                                         void* v_pool_layer, int64_t num_blocks, int block_size, int num_kv_heads,
+                                         int head_dim, const int64_t* block_tables, int64_t bt_stride,
+                                         int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
+                                         int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int flags,
+                                         int rank, int world, void* const* areas, int64_t area_bytes,
+                                         int64_t wait_limit_ns, void* workspace, size_t workspace_bytes,
+                                         void* stream) {
+  using namespace pa;
+  if (batch < 0 || (flags & ~PA_DECODE_EARLY_INPUTS)) return PA_ERR_INVALID;
+  if (world < 2 || world > PA_PEER_MAX_RANKS || rank < 0 || rank >= world || areas == nullptr) return PA_ERR_INVALID;
+  if (wait_limit_ns < 0 || wait_limit_ns > 2000000000LL) return PA_ERR_INVALID;
+  for (int r = 0; r < world; ++r)
+    if (areas[r] == nullptr || (reinterpret_cast<uintptr_t>(areas[r]) & 255)) return PA_ERR_INVALID;
+  if (batch == 0) return PA_OK;
+  const bool write = new_k != nullptr || new_v != nullptr || slot_mapping != nullptr;
+  if (write && (new_k == nullptr || new_v == nullptr || slot_mapping == nullptr)) return PA_ERR_INVALID;
+  if (write && ((reinterpret_cast<uintptr_t>(new_k) | reinterpret_cast<uintptr_t>(new_v)) & 15))
+    return PA_ERR_UNSUPPORTED;
+  if (dtype != PA_DTYPE_F16 && dtype != PA_DTYPE_BF16) return PA_ERR_UNSUPPORTED;
+  const Exchange xc{rank, world, areas, area_bytes, wait_limit_ns};
+  FusedWrite fw{new_k, new_v, slot_mapping};
+  bool fused = false;
+  const int r = decode_impl(q, q_s0, q_s1, k_pool_layer, v_pool_layer, num_blocks, block_size, num_kv_heads, head_dim,
+                            block_tables, bt_stride, bt_width, context_lens, out, o_s0, o_s1, batch, num_q_heads,
+                            scale, dtype, 0, workspace, workspace_bytes, stream, write ? &fw : nullptr, &fused, flags,
+                            -1, 1.f, 1.f, &xc);
+  if (r == PA_OK && write && !fused) return PA_ERR_UNSUPPORTED;  // not reached: the exchange needs the fused kernel
+  return r;
+}
+
 namespace pa {
 namespace {
 
@@ -1453,7 +1628,7 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
                 int64_t bt_stride, int64_t bt_width, const int64_t* context_lens, void* out, int64_t o_s0,
                 int64_t o_s1, int batch, int num_q_heads, float scale, int dtype, int partition_tokens,
                 void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused,
-                int flags, int kv_dtype, float k_scale, float v_scale) {
+                int flags, int kv_dtype, float k_scale, float v_scale, const Exchange* xc) {
   if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0 ||
       block_size <= 0 || num_blocks <= 0 || bt_width <= 0 || partition_tokens < 0 || (flags & ~PA_DECODE_EARLY_INPUTS))
     return PA_ERR_INVALID;
@@ -1485,6 +1660,7 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
     if (fused != nullptr) *fused = false;  // only the balanced kernel fuses the write
     return PA_OK;
   }
+  if (xc != nullptr && pl.kind != DecodePlan::kFlat) return PA_ERR_UNSUPPORTED;  // the exchange rides the combine
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
   if (ws == nullptr || workspace_bytes < pl.ws_bytes || (reinterpret_cast<uintptr_t>(ws) & 255))
     return PA_ERR_WORKSPACE;
@@ -1543,6 +1719,19 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
       p.k_pool = const_cast<void*>(k_pool_layer);
       p.v_pool = const_cast<void*>(v_pool_layer);
       p.num_slots = static_cast<int64_t>(num_blocks) * block_size;
+      for (int i = 0; i < PA_PEER_MAX_RANKS; ++i) p.xareas[i] = nullptr;
+      p.xrank = 0;
+      p.xworld = 0;
+      p.xline_bytes = 0;
+      p.xlimit_ns = kWaitLimitNs;
+      if (xc != nullptr) {
+        p.xrank = xc->rank;
+        p.xworld = xc->world;
+        p.xline_bytes = (int64_t)batch * p.SPS * 16 * (head_dim / 8) * 32;
+        if (256 + 2 * (int64_t)xc->world * p.xline_bytes > xc->area_bytes) return PA_ERR_CAPACITY;
+        for (int i = 0; i < xc->world; ++i) p.xareas[i] = static_cast<uint8_t*>(xc->areas[i]);
+        if (xc->wait_limit_ns > 0) p.xlimit_ns = static_cast<uint64_t>(xc->wait_limit_ns);
+      }
       if (fused != nullptr) *fused = fw != nullptr;
       const int g = pl.grid;
       using B16 = __nv_bfloat16;

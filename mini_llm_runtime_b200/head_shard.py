@@ -62,7 +62,8 @@ class PeerHeadGather:
     same sequence on every rank; they may be captured in a CUDA graph."""
 
     def __init__(self, group: dist.ProcessGroup | None, max_batch: int, heads_local: int, head_dim: int,
-                 dtype: torch.dtype, device: torch.device, wait_limit_ns: int = 0):
+                 dtype: torch.dtype, device: torch.device, wait_limit_ns: int = 0,
+                 kv_heads_local: int | None = None):
         lib = _lib.load()
         self.group = group
         self.world = dist.get_world_size(group)
@@ -76,6 +77,10 @@ class PeerHeadGather:
         nbytes = lib.pa_peer_gather_bytes(self.world, max_batch * heads_local * head_dim * esize)
         if nbytes == 0:
             raise ValueError("invalid peer all-gather size")
+        if kv_heads_local is not None:
+            # Room for the decode with the exchange fused into it as well.
+            nbytes = max(nbytes, lib.pa_decode_allgather_bytes(max_batch, kv_heads_local, heads_local, head_dim,
+                                                               self.world))
         # Above the caching allocator's 10 MB split limit the area gets a
         # segment (one cudaMalloc) of its own: its IPC handle is distinct from
         # every other area's, and a peer maps it exactly once.
@@ -166,12 +171,16 @@ class HeadShardedDecode:
         local_decode: Callable | None = None,
         transport: str = "peer",
         max_batch: int = 256,
+        fuse: bool = True,
     ):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.hq, self.hkv = num_q_heads, num_kv_heads
         self.q_slice, self.kv_slice = head_slices(num_q_heads, num_kv_heads, self.world, self.rank)
+        # With the package's own decode the exchange rides inside it
+        # (pa_paged_decode_allgather); a custom local_decode is followed by it.
+        self._fusable = fuse and local_decode is None and self.world > 1
         if local_decode is None:
             from .paged_attention import paged_attention_decode_batch_parallel as local_decode
         self.local_decode = local_decode
@@ -201,18 +210,31 @@ class HeadShardedDecode:
         b, hq_local, d = q_local.shape
         if hq_local * self.world != self.hq or k_pool_local.shape[2] * self.world != self.hkv:
             raise ValueError("q_local / pools do not hold this rank's share of the heads")
-        part = self.local_decode(q_local, k_pool_local, v_pool_local, block_tables, context_lens, block_size)
         if self.transport == "peer":
-            if self._peer is None or self._peer.dtype != part.dtype or b > self._peer.max_batch:
+            peer = self._peer
+            if peer is None or peer.dtype != q_local.dtype or b > peer.max_batch:
                 # Collective set-up: every rank reaches it at the same call
                 # (the same metadata on every rank).
-                if self._peer is not None:
-                    self._peer.close()
-                self._peer = PeerHeadGather(self.group, max(b, self.max_batch), hq_local, d, part.dtype,
-                                            part.device)
+                if peer is not None:
+                    peer.close()
+                peer = self._peer = PeerHeadGather(self.group, max(b, self.max_batch), hq_local, d, q_local.dtype,
+                                                   q_local.device, kv_heads_local=k_pool_local.shape[2])
             if out is None:
-                out = torch.empty((b, self.hq, d), dtype=part.dtype, device=part.device)
-            return self._peer(part, out)
+                out = torch.empty((b, self.hq, d), dtype=q_local.dtype, device=q_local.device)
+            if self._fusable:
+                from .paged_attention import decode_allgather_launch
+
+                lo = self.rank * hq_local
+                st = decode_allgather_launch(q_local, k_pool_local, v_pool_local, block_tables, context_lens,
+                                             block_size, out[:, lo:lo + hq_local], self.rank, self.world,
+                                             peer._areas, peer._nbytes, peer.wait_limit_ns)
+                if st == _lib.PA_OK:
+                    return out
+                # PA_ERR_UNSUPPORTED (nothing launched, same answer on every
+                # rank for the same shapes): decode, then the exchange kernel.
+            part = self.local_decode(q_local, k_pool_local, v_pool_local, block_tables, context_lens, block_size)
+            return peer(part, out)
+        part = self.local_decode(q_local, k_pool_local, v_pool_local, block_tables, context_lens, block_size)
         gathered = torch.empty((self.world, b, hq_local, d), dtype=part.dtype, device=part.device)
         if self._nccl:
             dist.all_gather_into_tensor(gathered, part.contiguous(), group=self.group)

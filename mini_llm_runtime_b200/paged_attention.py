@@ -238,6 +238,78 @@ def paged_attention_decode_batch_parallel(
     return _decode_launch(q, k_cache, v_cache, block_tables, seq_lens, out, 0, k_scale=k_scale, v_scale=v_scale)
 
 
+def decode_allgather_launch(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    block_tables: torch.Tensor,
+    seq_lens: torch.Tensor,
+    block_size: int,
+    out_local: torch.Tensor,
+    rank: int,
+    world: int,
+    areas,
+    area_bytes: int,
+    wait_limit_ns: int = 0,
+) -> int:
+    """Batched decode of this rank's heads with the all-gather of head outputs
+    fused into it (pa_paged_decode_allgather); KV-head-sharded decode.
+
+    ``out_local`` is this rank's head slice ``[:, rank*Hq:(rank+1)*Hq]`` of the
+    ``[B, world*Hq, D]`` output of all ranks; ``areas`` the ctypes array of every
+    rank's exchange area.  Returns 0, or PA_ERR_UNSUPPORTED (nothing launched)
+    when the call must take the unfused path; other errors raise.  The same
+    checks as paged_attention_decode_batch_parallel run first."""
+    if q.ndim != 3:
+        raise ValueError("q must have shape [B, Hq, D]")
+    _check_caches(k_cache, v_cache)
+    num_query_heads, num_kv_heads, head_dim = q.shape[1], k_cache.shape[2], q.shape[-1]
+    if head_dim != k_cache.shape[-1]:
+        raise ValueError("q and KV cache must have the same head_dim")
+    if num_query_heads % num_kv_heads != 0:
+        raise ValueError("num_query_heads must be divisible by num_kv_heads")
+    if len(block_tables) != q.shape[0] or len(seq_lens) != q.shape[0]:
+        raise ValueError("block_tables and seq_lens must match the batch size of q")
+    if block_size != k_cache.shape[1]:
+        raise ValueError("block_size does not match KV cache layout")
+    dev = _lib.require_cuda(q, k_cache, v_cache, out_local, what="paged decode with head all-gather")
+    if k_cache.dtype == _lib.FP8_DTYPE:
+        return _lib.PA_ERR_UNSUPPORTED
+    _pool_ok(k_cache, v_cache, q.dtype)
+    block_tables = _as_long(block_tables, dev)
+    seq_lens = _as_long(seq_lens, dev).contiguous()
+    if block_tables.ndim != 2:
+        raise ValueError("block_tables must have shape [B, max_num_blocks]")
+    if block_tables.stride(1) != 1:
+        block_tables = block_tables.contiguous()
+    if q.stride(2) != 1:
+        q = q.contiguous()
+    if tuple(out_local.shape) != tuple(q.shape) or out_local.dtype != q.dtype or out_local.stride(2) != 1:
+        raise ValueError("out_local must be this rank's [B, Hq, D] slice of the gathered output")
+    lib = _lib.load()
+    b, hq, d = q.shape
+    nb, bs, hkv, _ = k_cache.shape
+    code = _lib.dtype_code(q.dtype)
+    width = block_tables.shape[1]
+    ws_bytes = _lib.decode_workspace_bytes(b, hkv, hq, d, bs, width, 0, code)
+    if ws_bytes == 0:
+        raise ValueError("invalid decode arguments")
+    ws = _lib.decode_workspace(dev, ws_bytes, b, hq)
+    with _lib.device_guard(dev):
+        st = lib.pa_paged_decode_allgather(
+            q.data_ptr(), q.stride(0), q.stride(1), None, None, None,
+            k_cache.data_ptr(), v_cache.data_ptr(), nb, bs, hkv, d,
+            block_tables.data_ptr(), block_tables.stride(0), width, seq_lens.data_ptr(),
+            out_local.data_ptr(), out_local.stride(0), out_local.stride(1), b, hq, 1.0 / math.sqrt(d), code, 0,
+            rank, world, areas, area_bytes, wait_limit_ns, ws.data_ptr(), ws.numel(), _lib.stream_handle(dev),
+        )
+    if st == _lib.PA_ERR_UNSUPPORTED:
+        return st
+    _lib.check(st, "pa_paged_decode_allgather")
+    _lib.after_launch(dev)
+    return st
+
+
 def paged_attention_decode_split_kv(
     q: torch.Tensor,
     k_cache: torch.Tensor,

@@ -117,3 +117,28 @@ def test_peer_gather_sizes_and_host_checks():
     assert call(nbytes=256) == _lib.PA_ERR_CAPACITY         # area too small for two slots
     assert lib.pa_ipc_export(None, None, None) == _lib.PA_ERR_INVALID
     assert lib.pa_ipc_close(None) == _lib.PA_ERR_INVALID
+
+
+def test_decode_allgather_sizes_and_host_checks():
+    lib = _lib.load()
+    # Config 3 split over 2 ranks: B 8, one KV head and 7 query heads per rank,
+    # one segment per sequence, 16 rows x 8 column groups x 32 bytes of lines.
+    assert lib.pa_decode_allgather_bytes(8, 1, 7, 64, 2) == 256 + 2 * 2 * 8 * 16 * 8 * 32
+    # Two KV heads per segment (group of 7 <= 8): Hkv / 2 segments per sequence.
+    assert lib.pa_decode_allgather_bytes(4, 2, 14, 128, 4) == 256 + 2 * 4 * 4 * 16 * 16 * 32
+    assert lib.pa_decode_allgather_bytes(0, 1, 7, 64, 2) == 0
+    assert lib.pa_decode_allgather_bytes(8, 1, 7, 64, 1) == 256 + 2 * 8 * 16 * 8 * 32
+    assert lib.pa_decode_allgather_bytes(8, 2, 7, 64, 2) == 0  # Hq % Hkv != 0
+    fake = ctypes.c_void_p(4096)
+    areas = (ctypes.c_void_p * 2)(4096, 8192)
+
+    def call(rank=0, world=2, limit=0, flags=0, arr=areas):
+        return lib.pa_paged_decode_allgather(fake, 448, 64, None, None, None, fake, fake, 100, 16, 1, 64, fake, 8,
+                                             8, fake, fake, 896, 64, 8, 7, 0.125, 2, flags, rank, world, arr,
+                                             1 << 20, limit, fake, 1 << 20, None)
+
+    assert call(world=1) == _lib.PA_ERR_INVALID            # a one-rank exchange has no peer
+    assert call(rank=2) == _lib.PA_ERR_INVALID
+    assert call(limit=-5) == _lib.PA_ERR_INVALID
+    assert call(flags=8) == _lib.PA_ERR_INVALID
+    assert call(arr=(ctypes.c_void_p * 2)(4096, 8200)) == _lib.PA_ERR_INVALID  # areas must be 256-byte aligned

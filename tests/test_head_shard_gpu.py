@@ -1,8 +1,9 @@
 """KV-head-sharded decode on 2 GPUs: each rank decodes its KV heads with the
-CUDA kernels, and the all-gather of head outputs, over NVLink peer stores
-(pa_head_allgather) and over NCCL, must rebuild the oracle's unsharded result
-(BF16 tolerance), bit-identically between the two transports, call after call
-and under CUDA-graph replay.  Needs two GPUs; skipped with fewer."""
+CUDA kernels, and the all-gather of head outputs (fused into the decode's
+merge kernel, as a kernel of its own over NVLink peer stores, and over NCCL)
+must rebuild the oracle's unsharded result (BF16 tolerance), bit-identically
+between the three, call after call and under CUDA-graph replay.  Needs two
+GPUs; skipped with fewer."""
 
 import os
 import socket
@@ -38,8 +39,8 @@ def _rank_main(rank, world, port, result_path):
         q, k, v, tables, lens = case["np"]
         ref = torch.from_numpy(O.decode_batch(q, k, v, tables, lens, 16))
         checks, outs = {}, {}
-        for transport in ("peer", "collective"):
-            hs = HeadShardedDecode(14, 2, transport=transport, max_batch=4)
+        for transport, fuse in (("peer", True), ("peer-unfused", False), ("collective", True)):
+            hs = HeadShardedDecode(14, 2, transport=transport.split("-")[0], max_batch=4, fuse=fuse)
             ql = hs.local_queries(case["q"])
             kl, vl = shard_pool(case["k"], hs.kv_slice), shard_pool(case["v"], hs.kv_slice)
             for _ in range(3):  # the exchange alternates its two slots call by call
@@ -69,6 +70,7 @@ def _rank_main(rank, world, port, result_path):
                 del graph
             hs.close()
         checks["peer == collective"] = torch.equal(outs["peer"], outs["collective"])
+        checks["peer == unfused"] = torch.equal(outs["peer"], outs["peer-unfused"])
         flags = [None] * world
         dist.all_gather_object(flags, checks)
         if rank == 0:

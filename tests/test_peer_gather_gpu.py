@@ -74,3 +74,34 @@ def test_missing_peer_times_out_with_status(cuda_device):
     torch.cuda.synchronize()
     assert torch.equal(one, part)
     assert area[136:140].view(torch.int32).item() == 0
+
+
+def test_fused_decode_exchange_with_a_missing_peer(cuda_device):
+    """pa_paged_decode_allgather for "rank 0 of 2" whose peer area is its own:
+    this rank's heads equal the plain decode bit for bit, the peer's heads
+    never arrive, and the wait ends with PA_DEVICE_TIMEOUT_PEER in the area
+    and in the decode workspace, without a fault or a hang."""
+    from mini_llm_runtime_b200 import paged_attention_decode_batch_parallel
+    from mini_llm_runtime_b200.paged_attention import decode_allgather_launch
+    from tests.paged_inputs import make_decode_case
+
+    lib = _lib.load()
+    case = make_decode_case([700, 33, 4100], 7, 1, 64, 16, torch.bfloat16, cuda_device, seed=5)
+    b, hl, d = case["q"].shape
+    nbytes = lib.pa_decode_allgather_bytes(b, 1, hl, d, 2)
+    area = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    areas = (ctypes.c_void_p * 2)(area.data_ptr(), area.data_ptr())
+    out = torch.zeros(b, 2 * hl, d, device=cuda_device, dtype=torch.bfloat16)
+    try:
+        st = decode_allgather_launch(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16,
+                                     out[:, :hl], 0, 2, areas, nbytes, 20_000_000)
+        assert st == 0
+        torch.cuda.synchronize()
+        assert area[136:140].view(torch.int32).item() == _lib.PA_DEVICE_TIMEOUT_PEER
+        assert any(code == _lib.PA_DEVICE_TIMEOUT_PEER for _, code in _lib.device_status(cuda_device))
+        ref = paged_attention_decode_batch_parallel(case["q"], case["k"], case["v"], case["tables"], case["lens"], 16)
+        torch.cuda.synchronize()
+        assert torch.equal(out[:, :hl], ref)
+        assert torch.count_nonzero(out[:, hl:]) == 0
+    finally:
+        _lib.reset_device_status(cuda_device)
