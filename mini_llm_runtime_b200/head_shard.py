@@ -13,12 +13,14 @@ every rank.  Each rank streams 1/g of the KV bytes; the all-gather moves
 the collective is latency-bound, not bandwidth-bound.
 
 This is the one place an exchange between GPUs sits on the path.  By default
-(``transport="peer"`` on CUDA ranks) it is ``pa_head_allgather``: one kernel
-stores each rank's slice straight into every peer's memory over NVLink (CUDA
-IPC mappings set up once) as lines that carry the call's number, and polls
-(bounded) for the peers' lines: one launch and one NVLink crossing per layer.
-``transport="collective"`` runs ``torch.distributed`` all-gather instead (NCCL
-on GPUs, gloo on CPU ranks).  The reference runs one process on one device
+(``transport="peer"`` on CUDA ranks) it is fused into the decode
+(``pa_paged_decode_allgather``): the decode's merge kernel stores each CTA's
+finished output rows straight into every peer's memory over NVLink (CUDA IPC
+mappings set up once) as lines that carry the call's number, and polls
+(bounded) for the peers' rows.  Where that path is unsupported (or with
+``fuse=False``) the decode is followed by ``pa_head_allgather``, the same
+exchange as a kernel of its own.  ``transport="collective"`` runs
+``torch.distributed`` all-gather instead (NCCL on GPUs, gloo on CPU ranks).  The reference runs one process on one device
 (runtime/model_runner.py:146-288), so it has no counterpart; the per-rank math
 is its paged_attention_decode_batch_parallel
 (kernels/reference/paged_attention.py:178-254) on a head slice.
