@@ -20,9 +20,10 @@ from ._lib import PagedAttentionError, check_device_status, device_status, reset
 from .decode_graph import PagedDecodeGraph
 from .paged_kv_cache import PagedKVCache
 from .qwen2_attention import Qwen2Attention
-from .runner import ModelBatch, build_model_batch, execute_model_batch, swap_attention
+from .runner import DecodeStepGraph, ModelBatch, build_model_batch, execute_model_batch, swap_attention
 
 __all__ = [
+    "DecodeStepGraph",
     "ModelBatch",
     "PagedAttentionError",
     "PagedDecodeGraph",

@@ -237,6 +237,14 @@ def execute_model_batch(model, batch: ModelBatch, kv_cache: PagedKVCache) -> tor
     """Packed logits [T, vocab] of one scheduler step (model_runner.py:146-272),
     in the packed token order, with one batched chunk-prefill and one batched
     decode per layer."""
+    h, prefill_idx, decode_idx = _check_step(model, batch, kv_cache)
+    return _run_step(model, batch, kv_cache, _StepPlan(batch, h, prefill_idx, decode_idx, kv_cache.block_size))
+
+
+def _check_step(model, batch: ModelBatch, kv_cache: PagedKVCache):
+    """The reference's checks of one step (model_runner.py:146-244), on the
+    host metadata: (host metadata, prefill request indices, decode request
+    indices)."""
     if len(batch.request_phases) != len(batch.request_ids):
         raise ValueError("request_phases length must match request_ids")
     if not batch.request_ids:
@@ -323,8 +331,13 @@ def execute_model_batch(model, batch: ModelBatch, kv_cache: PagedKVCache) -> tor
                             "(call swap_attention(model) first)")
     if not isinstance(kv_cache, PagedKVCache):
         raise TypeError("kv_cache must be a mini_llm_runtime_b200.PagedKVCache")
+    return h, prefill_idx, decode_idx
 
-    plan = _StepPlan(batch, h, prefill_idx, decode_idx, bs)
+
+def _run_step(model, batch: ModelBatch, kv_cache: PagedKVCache, plan: "_StepPlan") -> torch.Tensor:
+    """The device work of a checked step: no host synchronisation, so it can
+    be captured in a CUDA graph."""
+    inner = model.model
     hidden = inner.embed_tokens(batch.input_token_ids)  # [T, hidden]
     for layer_idx, layer in enumerate(inner.layers):
         residual = hidden
@@ -346,6 +359,87 @@ def execute_model_batch(model, batch: ModelBatch, kv_cache: PagedKVCache) -> tor
         residual = hidden
         hidden = residual + layer.mlp(layer.post_attention_layernorm(hidden))
     return model.lm_head(inner.norm(hidden))
+
+
+class DecodeStepGraph:
+    """A whole decode step of the model in one CUDA graph: the embedding,
+    every layer's norms, projections, RoPE, KV write with paged decode, MLP,
+    then the final norm and LM head.  That is the reference's per-layer
+    decode loop (model/qwen2.py:1147-1156, run per step by
+    model_runner.py:146-288) replayed with one launch.
+
+    Built for ``num_requests`` decode requests with block tables of up to
+    ``table_width`` blocks.  ``run(batch)`` checks the step on the host as
+    ``execute_model_batch`` does, copies the batch's device tensors into the
+    graph's inputs and replays.  It returns the graph's logits
+    ``[num_requests, vocab]``, which the next run overwrites.
+
+    The first run captures the graph; its batch fixes whether the new tokens'
+    KV write is fused into the decode.  A later batch that needs the other
+    choice (a new token in a block shared with another sequence) runs
+    eagerly instead.  Capture runs the step once eagerly first: it writes the
+    same KV rows the replay writes, so the step's effect is unchanged.
+    """
+
+    def __init__(self, model, kv_cache: PagedKVCache, num_requests: int, table_width: int):
+        if num_requests <= 0 or table_width <= 0:
+            raise ValueError("num_requests and table_width must be positive")
+        self.model, self.kv_cache = model, kv_cache
+        self.num_requests, self.table_width = num_requests, table_width
+        dev = next(model.parameters()).device
+        if dev.type != "cuda":
+            raise ValueError("DecodeStepGraph needs a model on a CUDA device")
+        z = lambda: torch.zeros(num_requests, dtype=torch.long, device=dev)  # noqa: E731
+        self.tokens, self.positions, self.slots, self.lens = z(), z(), z(), z()
+        self.tables = torch.full((num_requests, table_width), -1, dtype=torch.long, device=dev)
+        self.qsl = torch.arange(num_requests + 1, dtype=torch.long, device=dev)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.logits: torch.Tensor | None = None
+        self._fused: bool | None = None
+        self._stream = torch.cuda.Stream(dev)
+
+    def run(self, batch: ModelBatch) -> torch.Tensor:
+        h, prefill_idx, decode_idx = _check_step(self.model, batch, self.kv_cache)
+        if prefill_idx or len(decode_idx) != self.num_requests:
+            raise ValueError(f"DecodeStepGraph runs steps of exactly {self.num_requests} decode requests")
+        w = batch.block_tables.shape[1]
+        if w > self.table_width:
+            raise ValueError(f"block_tables wider than the graph's {self.table_width} blocks")
+        bs = self.kv_cache.block_size
+        fused = new_token_blocks_private(h.context_lens, h.block_tables, bs)
+        if self.graph is not None and fused != self._fused:
+            return execute_model_batch(self.model, batch, self.kv_cache)
+        self.tokens.copy_(batch.input_token_ids)
+        self.positions.copy_(batch.positions)
+        self.slots.copy_(batch.slot_mapping)
+        self.lens.copy_(batch.context_lens)
+        self.tables.fill_(-1)
+        self.tables[:, :w].copy_(batch.block_tables)
+        if self.graph is None:
+            self._capture(h, fused)
+        self.graph.replay()
+        return self.logits
+
+    def _capture(self, h: BatchHostMeta, fused: bool) -> None:
+        n = self.num_requests
+        tables = np.full((n, self.table_width), -1, dtype=np.int64)
+        tables[:, :h.block_tables.shape[1]] = h.block_tables
+        host = BatchHostMeta(np.arange(n + 1, dtype=np.int64), h.context_lens.copy(), tables)
+        static = ModelBatch([f"decode{i}" for i in range(n)], self.tokens, self.positions, self.qsl,
+                            [RequestStatus.DECODING] * n, self.lens, self.tables, self.slots, host)
+        plan = _StepPlan(static, host, [], list(range(n)), self.kv_cache.block_size)
+        cur = torch.cuda.current_stream(self.tokens.device)
+        self._stream.wait_stream(cur)  # the staged inputs
+        with torch.cuda.stream(self._stream):
+            # Eager run first: the op workspaces of this stream exist before
+            # capture, and library kernels are loaded.
+            _run_step(self.model, static, self.kv_cache, plan)
+        self._stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self._stream):
+            self.logits = _run_step(self.model, static, self.kv_cache, plan)
+        cur.wait_stream(self._stream)
+        self.graph, self._fused = graph, fused
 
 
 class _StepPlan:

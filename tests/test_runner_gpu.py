@@ -117,3 +117,44 @@ def _reorder(b, order):
     return ModelBatch([b.request_ids[i] for i in order], b.input_token_ids[r], b.positions[r],
                       torch.from_numpy(nq).to(r.device), [b.request_phases[i] for i in order], b.context_lens[o],
                       b.block_tables[o], b.slot_mapping[r], host)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_decode_step_graph_replays_the_model_decode_step(cuda_device, dtype):
+    """The fixture's third step (decodes only) as one CUDA graph of the whole
+    model (DecodeStepGraph): its logits match the eager execute_model_batch
+    (FP32 within 1e-5, BF16 within 1e-2) and the reference runner's (FP32
+    within 1e-4), it writes the same KV rows, and replaying the same step
+    again gives the same logits bit for bit."""
+    from mini_llm_runtime_b200 import DecodeStepGraph
+
+    steps, _ = replay_outputs()
+    model = _model(dtype, cuda_device)
+    d = M.CONFIG["hidden_size"] // M.CONFIG["num_attention_heads"]
+
+    def cache_after_two_steps():
+        cache = PagedKVCache(M.CONFIG["num_hidden_layers"], M.NUM_BLOCKS, M.BLOCK_SIZE,
+                             M.CONFIG["num_key_value_heads"], d, dtype=dtype, device=cuda_device)
+        cache.k_cache.zero_()  # the pools start uninitialised; zeroed, they compare whole
+        cache.v_cache.zero_()
+        for out, _, _, _ in steps[:2]:
+            execute_model_batch(model, build_model_batch(out, M.BLOCK_SIZE, cuda_device), cache)
+        return cache
+
+    out3, _, want3, _ = steps[2]
+    with torch.no_grad():
+        eager_cache = cache_after_two_steps()
+        eager = execute_model_batch(model, build_model_batch(out3, M.BLOCK_SIZE, cuda_device), eager_cache).clone()
+        cache = cache_after_two_steps()
+        batch = build_model_batch(out3, M.BLOCK_SIZE, cuda_device)
+        g = DecodeStepGraph(model, cache, len(batch.request_ids), batch.block_tables.shape[1] + 3)
+        first = g.run(batch).clone()
+        again = g.run(build_model_batch(out3, M.BLOCK_SIZE, cuda_device)).clone()
+        torch.cuda.synchronize()
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    torch.testing.assert_close(first, eager, rtol=tol, atol=tol)
+    assert torch.equal(first, again)
+    torch.testing.assert_close(cache.k_cache, eager_cache.k_cache, rtol=tol, atol=tol)
+    torch.testing.assert_close(cache.v_cache, eager_cache.v_cache, rtol=tol, atol=tol)
+    if dtype == torch.float32:
+        np.testing.assert_allclose(first.float().cpu().numpy(), want3, rtol=1e-4, atol=1e-4)
