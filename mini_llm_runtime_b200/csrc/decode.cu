@@ -42,6 +42,11 @@
 
 #include "attn_generic.cuh"
 
+// The decode kernels' K/V copies carry an L2 evict-first policy (1) or none
+// (0): the pools are read once per call.
+#ifndef PA_DECODE_KV_EVICT_FIRST
+#define PA_DECODE_KV_EVICT_FIRST 1
+#endif
 // Early-inputs launches warm L2 with the first piece's query rows before the
 // wait for the previous kernel (1) or not (0).
 #ifndef PA_DECODE_Q_PREFETCH
@@ -597,6 +602,12 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
   __shared__ int nruns_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+#if PA_DECODE_KV_EVICT_FIRST
+  // The pools are streamed once per call: their lines leave L2 first, so
+  // the stream does not evict the queries, metadata, records and code that
+  // this layer's tail and the next layer read again.
+  const uint64_t kv_policy = l2_evict_first_policy();
+#endif
   uint8_t* ring = smem + warp * STAGES * C::kStageBytes;
   uint64_t* wbar = bars + warp * STAGES;
   // Shared-memory set-up needs no global data: it overlaps the previous
@@ -699,8 +710,14 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
       for (int ct = 0; ct < C::kColTiles; ++ct)
 #pragma unroll
         for (int h = 0; h < PK; ++h) {
+#if PA_DECODE_KV_EVICT_FIRST
+          tma_load_3d_hint(st + (ct * PK + h) * kTileX, &tmap_k, &wbar[stage], ct * 64, kv + h, y, kv_policy);
+          tma_load_3d_hint(st + ((C::kColTiles + ct) * PK + h) * kTileX, &tmap_v, &wbar[stage], ct * 64, kv + h, y,
+                           kv_policy);
+#else
           tma_load_3d(st + (ct * PK + h) * kTileX, &tmap_k, &wbar[stage], ct * 64, kv + h, y);
           tma_load_3d(st + ((C::kColTiles + ct) * PK + h) * kTileX, &tmap_v, &wbar[stage], ct * 64, kv + h, y);
+#endif
         }
     }
   };
@@ -1188,6 +1205,9 @@ __global__ void __launch_bounds__(NW * 32) decode_split_kernel(const __grid_cons
   __shared__ int last_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+#if PA_DECODE_KV_EVICT_FIRST
+  const uint64_t kv_policy = l2_evict_first_policy();  // pools streamed once
+#endif
   const int b = blockIdx.z, split = blockIdx.x;
   const int head_tiles = (p.group + 15) >> 4;
   const int kvh = blockIdx.y / head_tiles, ht = blockIdx.y - kvh * head_tiles;
@@ -1221,8 +1241,13 @@ __global__ void __launch_bounds__(NW * 32) decode_split_kernel(const __grid_cons
     mbar_arrive_expect_tx(&wbar[stage], C::kStageBytes);
 #pragma unroll
     for (int ct = 0; ct < C::kColTiles; ++ct) {
+#if PA_DECODE_KV_EVICT_FIRST
+      tma_load_3d_hint(st + ct * kTileBytes, &tmap_k, &wbar[stage], ct * 64, kvh, y, kv_policy);
+      tma_load_3d_hint(st + (C::kColTiles + ct) * kTileBytes, &tmap_v, &wbar[stage], ct * 64, kvh, y, kv_policy);
+#else
       tma_load_3d(st + ct * kTileBytes, &tmap_k, &wbar[stage], ct * 64, kvh, y);
       tma_load_3d(st + (C::kColTiles + ct) * kTileBytes, &tmap_v, &wbar[stage], ct * 64, kvh, y);
+#endif
     }
   };
   if (lane == 0) {
