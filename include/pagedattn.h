@@ -58,6 +58,7 @@ extern "C" {
 
 /* Flags of pa_paged_decode_ex. */
 #define PA_DECODE_EARLY_INPUTS 1 /* metadata and pools may be read before the PDL wait */
+#define PA_DECODE_EARLY_QUERY 2  /* with EARLY_INPUTS: q may be read before it too */
 
 /* Ranks and IPC handle size of the peer head all-gather. */
 #define PA_PEER_MAX_RANKS 8
@@ -229,6 +230,14 @@ PA_API int pa_paged_decode_write(const void* q, int64_t q_s0, int64_t q_s1, cons
  * decode in a captured multi-layer step.  q, new_k and new_v are still read,
  * and everything is written, only after the wait.  Without the flag the
  * kernel waits before its first global access.
+ *
+ * flags |= PA_DECODE_EARLY_QUERY (only with PA_DECODE_EARLY_INPUTS): the
+ * caller also vouches that q is complete when the kernel is launched — no
+ * kernel that may still be running writes it (q comes from a copy or a
+ * kernel the launch is fully ordered after, as in a captured step whose
+ * per-layer queries are inputs).  The balanced kernel then loads its first
+ * query rows before the wait as well.  Not for a model's layer loop, where
+ * the kernel just before computes q.
  */
 PA_API int pa_paged_decode_ex(const void* q, int64_t q_s0, int64_t q_s1, const void* new_k, const void* new_v,
                               const int64_t* slot_mapping, void* k_pool_layer, void* v_pool_layer,

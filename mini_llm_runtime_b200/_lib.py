@@ -24,6 +24,7 @@ PA_ERR_CUDA = -3
 PA_ERR_WORKSPACE = -4
 PA_ERR_CAPACITY = -5
 PA_DECODE_EARLY_INPUTS = 1
+PA_DECODE_EARLY_QUERY = 2
 PA_DEVICE_TIMEOUT_TMA = 101
 PA_DEVICE_TIMEOUT_MMA = 102
 PA_DEVICE_TIMEOUT_PEER = 103

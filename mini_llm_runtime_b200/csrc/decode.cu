@@ -473,6 +473,7 @@ __device__ __forceinline__ void axpy8(float wt, float4 v0, float4 v1, float* acc
 // of it.
 // ===========================================================================
 constexpr int kFlatMaxBatch = 1024;
+constexpr int kDecodeFlags = PA_DECODE_EARLY_INPUTS | PA_DECODE_EARLY_QUERY;  // accepted flag bits
 
 struct FlatParams {
   const void* q;
@@ -486,6 +487,7 @@ struct FlatParams {
   float scale_log2;
   int grid;     // CTAs of the main kernel
   int early;    // PA_DECODE_EARLY_INPUTS: read metadata and pools before the PDL wait
+  int early_q;  // PA_DECODE_EARLY_QUERY (with early): load the first query rows before it too
   float out_scale;  // output factor: 1, or the V scale of an FP8 pool
   float k_scale, v_scale;  // FP8 pools: the fused write stores x / scale
   float* part;  // [grid][2][16][D + 4] records of segments shared with other CTAs
@@ -723,31 +725,38 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
   };
   int issued = 0;
   for (; issued < STAGES && issued < nj; ++issued) issue(issued);
+  const TQ* qbase = reinterpret_cast<const TQ*>(p.q);
+  WS ws;
+  Seg pc{};
+  if (nj > 0) pc = seg_at(pre, p.B, p.SPS, lo);
+  if (p.early_q && nj > 0) {
+    // The caller vouches that q is complete at launch: the first piece's
+    // query fragments load now, and the first MMAs need nothing from after
+    // the wait.
+    int kvh0, h0, hn;
+    seg_heads<PK>(p, pc.segx, kvh0, h0, hn);
+    WS::template load_q<TQ>(ws.qa, qbase + (int64_t)pc.b * p.q_s0, p.q_s1, h0, p.group, hn, lane);
+  }
 #if PA_DECODE_Q_PREFETCH
-  if (p.early && nj > 0) {
+  if (p.early && !p.early_q && nj > 0) {
     // The first piece's query rows go to L2 while the previous kernel
     // finishes, so their load after the wait hits L2 instead of queueing in
     // HBM behind every CTA's first ring copies.
-    const Seg s0 = seg_at(pre, p.B, p.SPS, lo);
     int kvh0, h0, hn;
-    seg_heads<PK>(p, s0.segx, kvh0, h0, hn);
+    seg_heads<PK>(p, pc.segx, kvh0, h0, hn);
     constexpr int kLines = (D * (int)sizeof(TQ) + 127) / 128;
-    const TQ* qrow = reinterpret_cast<const TQ*>(p.q) + (int64_t)s0.b * p.q_s0;
+    const TQ* qrow = qbase + (int64_t)pc.b * p.q_s0;
     for (int i = lane; i < hn * kLines; i += 32)
       prefetch_l2(qrow + (int64_t)(h0 + i / kLines) * p.q_s1 + (i % kLines) * (128 / (int)sizeof(TQ)));
   }
 #endif
   if (p.early) grid_dep_wait();
 
-  const TQ* qbase = reinterpret_cast<const TQ*>(p.q);
   TQ* out = reinterpret_cast<TQ*>(p.out);
-  WS ws;
   int jc = 0;  // sub-blocks of this slice consumed so far
   bool ok = true;
   int first_sid = -1, last_sid = -1;
-  Seg pc{};
-  if (nj > 0) {
-    pc = seg_at(pre, p.B, p.SPS, lo);
+  if (!p.early_q && nj > 0) {
     int kvh0, h0, hn;
     seg_heads<PK>(p, pc.segx, kvh0, h0, hn);
     WS::template load_q<TQ>(ws.qa, qbase + (int64_t)pc.b * p.q_s0, p.q_s1, h0, p.group, hn, lane);
@@ -1578,7 +1587,7 @@ extern "C" int pa_paged_decode_ex(const void* q, int64_t q_s0, int64_t q_s1, con
                                   int num_q_heads, float scale, int dtype, int partition_tokens, int flags,
                                   void* workspace, size_t workspace_bytes, void* stream) {
   using namespace pa;
-  if (batch < 0 || (flags & ~PA_DECODE_EARLY_INPUTS)) return PA_ERR_INVALID;
+  if (batch < 0 || (flags & ~kDecodeFlags)) return PA_ERR_INVALID;
   if (batch == 0) return PA_OK;
   const bool write = new_k != nullptr || new_v != nullptr || slot_mapping != nullptr;
   if (!write)
@@ -1623,7 +1632,7 @@ extern "C" int pa_paged_decode_allgather(const void* q, int64_t q_s0, int64_t q_
                                          int64_t wait_limit_ns, void* workspace, size_t workspace_bytes,
                                          void* stream) {
   using namespace pa;
-  if (batch < 0 || (flags & ~PA_DECODE_EARLY_INPUTS)) return PA_ERR_INVALID;
+  if (batch < 0 || (flags & ~kDecodeFlags)) return PA_ERR_INVALID;
   if (world < 2 || world > PA_PEER_MAX_RANKS || rank < 0 || rank >= world || areas == nullptr) return PA_ERR_INVALID;
   if (wait_limit_ns < 0 || wait_limit_ns > 2000000000LL) return PA_ERR_INVALID;
   for (int r = 0; r < world; ++r)
@@ -1655,7 +1664,7 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
                 void* workspace, size_t workspace_bytes, void* stream, const FusedWrite* fw, bool* fused,
                 int flags, int kv_dtype, float k_scale, float v_scale, const Exchange* xc) {
   if (batch < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads != 0 || head_dim <= 0 ||
-      block_size <= 0 || num_blocks <= 0 || bt_width <= 0 || partition_tokens < 0 || (flags & ~PA_DECODE_EARLY_INPUTS))
+      block_size <= 0 || num_blocks <= 0 || bt_width <= 0 || partition_tokens < 0 || (flags & ~kDecodeFlags))
     return PA_ERR_INVALID;
   if (batch == 0) return PA_OK;
   if (q == nullptr || k_pool_layer == nullptr || v_pool_layer == nullptr || block_tables == nullptr ||
@@ -1733,6 +1742,7 @@ int decode_impl(const void* q, int64_t q_s0, int64_t q_s1, const void* k_pool_la
       p.scale_log2 = scale_log2;
       p.grid = pl.grid;
       p.early = (flags & PA_DECODE_EARLY_INPUTS) ? 1 : 0;
+      p.early_q = p.early && (flags & PA_DECODE_EARLY_QUERY) ? 1 : 0;
       p.out_scale = v_scale;
       p.k_scale = k_scale;
       p.v_scale = v_scale;
@@ -1867,7 +1877,7 @@ extern "C" int pa_paged_decode_fp8(const void* q, int64_t q_s0, int64_t q_s1, co
                                    int partition_tokens, int flags, void* workspace, size_t workspace_bytes,
                                    void* stream) {
   using namespace pa;
-  if (batch < 0 || (flags & ~PA_DECODE_EARLY_INPUTS)) return PA_ERR_INVALID;
+  if (batch < 0 || (flags & ~kDecodeFlags)) return PA_ERR_INVALID;
   if (batch == 0) return PA_OK;
   const bool write = new_k != nullptr || new_v != nullptr || slot_mapping != nullptr;
   if (write) {

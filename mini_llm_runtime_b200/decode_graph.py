@@ -100,8 +100,11 @@ class PagedDecodeGraph:
         # Inside the graph a layer's decode follows the previous layer's
         # decode (or the input copy), which writes no metadata and no pool
         # row of this layer: its kernel may start on them before that one
-        # ends (PA_DECODE_EARLY_INPUTS).
-        self._flags = _lib.PA_DECODE_EARLY_INPUTS if early_inputs else 0
+        # ends (PA_DECODE_EARLY_INPUTS).  Its queries are inputs of the step,
+        # copied before the replay or by a copy the layer's kernel is fully
+        # ordered after, so they may be read that early too
+        # (PA_DECODE_EARLY_QUERY).
+        self._flags = (_lib.PA_DECODE_EARLY_INPUTS | _lib.PA_DECODE_EARLY_QUERY) if early_inputs else 0
         self.scale = (1.0 / math.sqrt(cache.head_dim)) if scale is None else float(scale)
         L, B, H, D, HKV = len(self.layers), batch, num_q_heads, cache.head_dim, cache.num_kv_heads
         dt = qdt

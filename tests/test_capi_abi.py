@@ -75,6 +75,22 @@ def test_bad_arguments_rejected_on_host(call):
     assert call(_lib.load()) == _lib.PA_ERR_INVALID
 
 
+def test_decode_flags_match_header_and_unknown_bits_are_rejected():
+    text = (ROOT / "include" / "pagedattn.h").read_text()
+    defined = {m[0]: int(m[1]) for m in re.findall(r"#define\s+(PA_DECODE_\w+)\s+(\d+)", text)}
+    assert defined == {"PA_DECODE_EARLY_INPUTS": _lib.PA_DECODE_EARLY_INPUTS,
+                       "PA_DECODE_EARLY_QUERY": _lib.PA_DECODE_EARLY_QUERY}
+    lib = _lib.load()
+    fake = ctypes.c_void_p(4096)
+
+    def call(flags):
+        return lib.pa_paged_decode_ex(fake, 448, 64, None, None, None, fake, fake, 100, 16, 1, 64, fake, 8, 8, fake,
+                                      fake, 896, 64, 8, 7, 0.125, 2, 0, flags, fake, 1 << 20, None)
+
+    assert call(4) == _lib.PA_ERR_INVALID
+    assert call(_lib.PA_DECODE_EARLY_INPUTS | 4) == _lib.PA_ERR_INVALID
+
+
 def test_zero_sized_calls_are_noops():
     lib = _lib.load()
     assert lib.pa_kv_scatter(None, 0, 0, 0, None, 0, 0, 0, 0, None, 1, 0, None, None, 64, 2, 64, 0, None) == 0
