@@ -627,7 +627,8 @@ __global__ void __launch_bounds__(NW * 32, CTAS) decode_flat_kernel(const __grid
   // caller vouches that it writes none of the metadata and pools
   // (PA_DECODE_EARLY_INPUTS), only before the first read of q / new_k /
   // new_v and the first write, so the start-up (scan, block-table loads, the
-  // first TMA copies) overlaps the previous kernel's tail.  Let the next PDL
+  // first TMA copies) overlaps the previous kernel's tail.  With
+  // PA_DECODE_EARLY_QUERY the first query rows are read before it as well.  Let the next PDL
   // kernel launch early either way (it waits for this one).
   if (!p.early) grid_dep_wait();
   grid_dep_launch();
