@@ -201,6 +201,15 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return pol;
 }
 
+// Number of the next call of a peer exchange, from the last one made: the
+// exchange areas start zeroed and the call number marks arrived lines, so it
+// is never 0 (after 0xffffffff comes 2, which keeps the slot parity n & 1
+// alternating).
+__device__ __forceinline__ uint32_t next_call_number(uint32_t last) {
+  const uint32_t n = last + 1u;
+  return n == 0u ? 2u : n;
+}
+
 // Cache hint: bring the 128-byte line holding `ptr` into L2.  It reads no
 // value, so it may precede the wait for the kernel that writes the line: that
 // write lands in the same L2 line.

@@ -1024,7 +1024,7 @@ __global__ void __launch_bounds__(kCombineThreads, 8) decode_combine_kernel(Flat
   const int hh = row_head<PK>(r, p.group, hn);
   grid_dep_wait();  // the main kernel's records (and outputs) are complete and visible
   if constexpr (XCHG) {
-    if (tid == 0) call_s = *reinterpret_cast<volatile uint32_t*>(p.xareas[p.xrank] + 132) + 1u;
+    if (tid == 0) call_s = next_call_number(*reinterpret_cast<volatile uint32_t*>(p.xareas[p.xrank] + 132));
   }
   float mrun = -INFINITY, lrun = 0.f;
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};

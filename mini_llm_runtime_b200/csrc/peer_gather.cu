@@ -21,6 +21,8 @@
 //   [256, ...)   2 slots x world x 2 * slice bytes of lines; call n uses slot
 //                n & 1, so a peer that runs one call ahead writes the other
 //                slot, and a line left from call n - 2 reads as not arrived.
+//                Call numbers are never 0 (next_call_number), so a line never
+//                written since the area was zeroed never reads as arrived.
 // A peer can run at most one call ahead: it finishes a call only after it
 // has received this rank's lines of that call, which this rank stores only
 // after it has finished the call before.
@@ -72,7 +74,7 @@ __global__ void __launch_bounds__(kGatherThreads) head_allgather_kernel(GatherPa
   uint32_t* calls = arrivals + 1;
   int* status = reinterpret_cast<int*>(mine + 136);
   __shared__ uint32_t call_s;
-  if (threadIdx.x == 0) call_s = *reinterpret_cast<volatile uint32_t*>(calls) + 1u;
+  if (threadIdx.x == 0) call_s = next_call_number(*reinterpret_cast<volatile uint32_t*>(calls));
   __syncthreads();
   const uint32_t n = call_s;
   const int64_t lines_per_rank = 2 * p.slice_bytes;  // bytes of lines per rank's slice

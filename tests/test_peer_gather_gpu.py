@@ -76,6 +76,36 @@ def test_missing_peer_times_out_with_status(cuda_device):
     assert area[136:140].view(torch.int32).item() == 0
 
 
+def test_call_numbers_skip_zero_at_the_wrap(cuda_device):
+    """The 32-bit call counter goes from 0xffffffff to 2, never to 0. The
+    area's lines start zeroed, so a call numbered 0 would take a missing
+    peer's never-written lines for arrived ones."""
+    lib = _lib.load()
+    b, hl, d = 4, 7, 64
+    part = torch.randn(b, hl, d, device=cuda_device).to(torch.bfloat16)
+    one_bytes = lib.pa_peer_gather_bytes(1, b * hl * d * 2)
+    area = torch.zeros(one_bytes, dtype=torch.uint8, device=cuda_device)
+    area[132:136].view(torch.int32).fill_(-2)  # last call 0xfffffffe
+    for expect in (-1, 2):  # 0xffffffff, then 2
+        out = torch.zeros(b, hl, d, device=cuda_device, dtype=torch.bfloat16)
+        assert _call(lib, part, out, [area], one_bytes, 0, 1) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out, part)
+        assert area[128:140].view(torch.int32).tolist() == [0, expect, 0]
+    # "Rank 0 of 2" whose peer area is its own, at the wrap: the peer's lines
+    # were never written and must not read as arrived.
+    two_bytes = lib.pa_peer_gather_bytes(2, b * hl * d * 2)
+    area2 = torch.zeros(two_bytes, dtype=torch.uint8, device=cuda_device)
+    area2[132:136].view(torch.int32).fill_(-1)  # last call 0xffffffff
+    out = torch.zeros(b, 2 * hl, d, device=cuda_device, dtype=torch.bfloat16)
+    assert _call(lib, part, out, [area2, area2], two_bytes, 0, 2, limit_ns=20_000_000) == 0
+    torch.cuda.synchronize()
+    assert area2[136:140].view(torch.int32).item() == _lib.PA_DEVICE_TIMEOUT_PEER
+    assert area2[132:136].view(torch.int32).item() == 2
+    assert torch.equal(out[:, :hl], part)
+    assert torch.count_nonzero(out[:, hl:]) == 0
+
+
 def test_fused_decode_exchange_with_a_missing_peer(cuda_device):
     """pa_paged_decode_allgather for "rank 0 of 2" whose peer area is its own:
     this rank's heads equal the plain decode bit for bit, the peer's heads
